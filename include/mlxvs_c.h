@@ -1,0 +1,204 @@
+/*
+ * mlxvs_b200 C API: exact k-nearest-neighbor search on NVIDIA B200 (sm_100a).
+ *
+ * Drop-in for the brute-force part of mlxVS's C API
+ * (include/mlxvs/mlxvs_c.h in the reference).  Conventions follow it:
+ *   - every function returns MLXVS_OK (0) or an error code, and
+ *     mlxvs_last_error() then describes the failure (per thread; "" after a
+ *     success)                                   ref: src/c_api.cpp:28-47
+ *   - host-memory entry points take row-major host arrays, copy the inputs
+ *     and write the outputs into buffers the caller owns
+ *   - ids are int32 [nq, k], -1 where fewer than k rows exist; distances are
+ *     float32 [nq, k]: squared L2 (ascending, +inf where missing), or the
+ *     inner product / cosine similarity (descending, -inf where missing)
+ *   - ties keep the lower id (ref: src/kernels.h:20-23)
+ *
+ * Entry points marked "device" take CUDA device pointers and a cudaStream_t
+ * (as void*, NULL = the legacy default stream); they enqueue work and return
+ * without waiting, except where noted.  Errors found by the kernels
+ * themselves are reported by mlxvs_device_synchronize().
+ */
+#ifndef MLXVS_B200_C_H
+#define MLXVS_B200_C_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLXVS_C_API __attribute__((visibility("default")))
+
+/** The C API's version: major * 10000 + minor (ref: mlxvs_c.h:25). */
+#define MLXVS_C_API_VERSION 100
+
+/* ref: include/mlxvs/mlxvs_c.h:27-35 (same values) */
+typedef enum {
+  MLXVS_OK = 0,
+  /** An argument was out of range (mlxvs_last_error says which). */
+  MLXVS_ERROR_INVALID_ARGUMENT = 1,
+  /** Kept for value compatibility; the search functions do no file I/O. */
+  MLXVS_ERROR_IO = 2,
+  /** Anything else: no CUDA device, out of device memory, a kernel error. */
+  MLXVS_ERROR_INTERNAL = 3,
+} mlxvs_status;
+
+/* ref: include/mlxvs/mlxvs_c.h:37-45 (same values) */
+typedef enum {
+  /** Dot product, larger is closer. */
+  MLXVS_INNER_PRODUCT = 0,
+  /** Squared Euclidean distance, smaller is closer. */
+  MLXVS_L2 = 1,
+  /** Cosine similarity, larger is closer. */
+  MLXVS_COSINE = 2,
+} mlxvs_metric;
+
+/** Candidate-key lists produced by the *_keys_device functions hold
+ * Hamming keys when merged with this kind (not a metric of
+ * mlxvs_brute_force_knn). */
+#define MLXVS_KIND_HAMMING 3
+
+/** The last error of this thread, or "" after a success.
+ * ref: include/mlxvs/mlxvs_c.h:105-106, src/c_api.cpp:190-192 */
+MLXVS_C_API const char* mlxvs_last_error(void);
+
+/** The library version, such as "0.16.1-b200".
+ * ref: include/mlxvs/mlxvs_c.h:108-109, src/c_api.cpp:194-196 */
+MLXVS_C_API const char* mlxvs_version(void);
+
+/**
+ * Exact k-nearest neighbors of nq queries among n base rows (float32,
+ * row-major, host memory).  1 <= k <= 256; distances may be NULL.
+ * Replaces: mlxvs_brute_force_knn, include/mlxvs/mlxvs_c.h:247-256,
+ * src/c_api.cpp:468-489 (same signature and semantics).
+ */
+MLXVS_C_API int mlxvs_brute_force_knn(
+    const float* base,
+    int64_t n,
+    const float* queries,
+    int64_t nq,
+    int32_t d,
+    int32_t k,
+    mlxvs_metric metric,
+    int32_t* ids,
+    float* distances);
+
+/**
+ * Exact k-NN by Hamming distance of bit-packed rows uint8 [n, bytes] and
+ * queries uint8 [nq, bytes] (host memory).  Distances are the Hamming
+ * distances as float32, ascending, +inf where missing; ties keep the lower
+ * id.  1 <= k <= 256.
+ * Replaces: mlxvs::hamming_knn, include/mlxvs/mlxvs.h:780-784 and
+ * src/ivf.cpp:1343-1403 (the reference has no C entry for it).
+ */
+MLXVS_C_API int mlxvs_hamming_knn(
+    const uint8_t* rows,
+    int64_t n,
+    const uint8_t* queries,
+    int64_t nq,
+    int32_t bytes,
+    int32_t k,
+    int32_t* ids,
+    float* distances);
+
+/**
+ * mlxvs_brute_force_knn on device pointers, enqueued on stream.
+ * Replaces: mlxvs::brute_force_knn, include/mlxvs/mlxvs.h:59-65 (the C++
+ * entry the Python binding python/bindings.cpp:37-47 calls).  The inputs
+ * stay untouched; scratch memory comes from the device's stream-ordered
+ * pool.  Synchronizes with the host once, after the input-conversion
+ * kernels, to choose the exact fp16 path or the split-fp16 path.
+ */
+MLXVS_C_API int mlxvs_brute_force_knn_device(
+    const float* base,
+    int64_t n,
+    const float* queries,
+    int64_t nq,
+    int32_t d,
+    int32_t k,
+    mlxvs_metric metric,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
+/** mlxvs_hamming_knn on device pointers, enqueued on stream.
+ * Replaces: mlxvs::hamming_knn, include/mlxvs/mlxvs.h:780-784. */
+MLXVS_C_API int mlxvs_hamming_knn_device(
+    const uint8_t* rows,
+    int64_t n,
+    const uint8_t* queries,
+    int64_t nq,
+    int32_t bytes,
+    int32_t k,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
+/**
+ * One shard of a row-sharded search: the k best candidates of every query
+ * among these n base rows, as 64-bit keys [nq, k], best first, whose ids are
+ * id_offset + row.  A key is (order_bits(score) << 32) | (uint32)~id, where
+ * order_bits maps a float to an unsigned int of the same order (ref:
+ * src/kernels.h:16-19) and score is the reference's pre-distance score
+ * (L2: 2 q.b - |b|^2, ref src/knn.cpp:111-116; IP: q.b; cosine: the cosine);
+ * larger keys are better and 0 is an empty slot.
+ * Replaces: the per-tile step of src/knn.cpp:104-121 across devices.
+ */
+MLXVS_C_API int mlxvs_knn_keys_device(
+    const float* base,
+    int64_t n,
+    const float* queries,
+    int64_t nq,
+    int32_t d,
+    int32_t k,
+    mlxvs_metric metric,
+    int64_t id_offset,
+    uint64_t* keys,
+    void* stream);
+
+/** Hamming shard: keys of score -distance (see mlxvs_knn_keys_device).
+ * Replaces: the tile step of src/ivf.cpp:1370-1387 across devices. */
+MLXVS_C_API int mlxvs_hamming_keys_device(
+    const uint8_t* rows,
+    int64_t n,
+    const uint8_t* queries,
+    int64_t nq,
+    int32_t bytes,
+    int32_t k,
+    int64_t id_offset,
+    uint64_t* keys,
+    void* stream);
+
+/**
+ * Merges num_lists key lists laid out [num_lists][nq][k] into the k best per
+ * query (ties keep the lower id) and converts them to ids and distances of
+ * the given kind (an mlxvs_metric, or MLXVS_KIND_HAMMING).  For MLXVS_L2 the
+ * distance is max(|q|^2 - score, 0) (ref: src/knn.cpp:122-131), so queries
+ * [nq, d] must be given; otherwise queries may be NULL.
+ * Replaces: the cross-tile merge of src/knn.cpp:117 / src/ivf.cpp:1388-1402,
+ * here also across devices.
+ */
+MLXVS_C_API int mlxvs_merge_keys_device(
+    const uint64_t* lists,
+    int32_t num_lists,
+    int64_t nq,
+    int32_t k,
+    int32_t kind,
+    const float* queries,
+    int32_t d,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
+/**
+ * Waits for stream and reports any error the library's kernels recorded on
+ * the current device since the last call (a bounded wait that gave up).
+ * Not in the reference (MLX reports errors at mx::eval).
+ */
+MLXVS_C_API int mlxvs_device_synchronize(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXVS_B200_C_H */

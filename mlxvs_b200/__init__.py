@@ -1,0 +1,315 @@
+"""mlxvs_b200: exact k-nearest-neighbor search on NVIDIA B200 (sm_100a).
+
+A drop-in for mlxVS's exact k-NN entry points (python/mlxvs/__init__.py:106-115
+of the reference):
+
+    ids, distances = brute_force_knn(base, queries, k, metric="l2")
+    ids, distances = hamming_knn(rows, queries, k)
+
+NumPy arrays (or anything array-like) go through the C API's host-memory
+entry points and come back as NumPy arrays; CUDA torch tensors stay on the
+device and come back as torch tensors on the same device, computed on the
+current torch stream (or `stream=`).
+
+ids are int32 [nq, k], -1 where fewer than k rows exist; distances are
+float32 [nq, k]: squared L2 ascending (+inf where missing), inner product or
+cosine similarity descending (-inf where missing).  Ties keep the lower id.
+
+Everything runs in libmlxvs_b200.so (hand-written sm_100a kernels); there is
+no CPU fallback: without the library or a B200 the calls raise.
+"""
+
+import ctypes
+import enum
+import os
+
+import numpy as np
+
+__all__ = [
+    "Metric",
+    "brute_force_knn",
+    "hamming_knn",
+    "knn_keys",
+    "hamming_keys",
+    "merge_keys",
+    "library_path",
+    "version",
+]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libmlxvs_b200.so")
+_lib = None
+
+
+class Metric(enum.IntEnum):
+    """How two rows compare (the reference's mlxvs.Metric, same values)."""
+
+    inner_product = 0
+    l2 = 1
+    cosine = 2
+
+
+KIND_HAMMING = 3
+
+
+def library_path():
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise RuntimeError(
+            "mlxvs_b200: libmlxvs_b200.so is not built (python -m mlxvs_b200.build)")
+    lib = ctypes.CDLL(_LIB_PATH)
+    p, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    sig = {
+        "mlxvs_brute_force_knn": [p, i64, p, i64, i32, i32, ctypes.c_int, p, p],
+        "mlxvs_hamming_knn": [p, i64, p, i64, i32, i32, p, p],
+        "mlxvs_brute_force_knn_device": [p, i64, p, i64, i32, i32, ctypes.c_int, p, p, p],
+        "mlxvs_hamming_knn_device": [p, i64, p, i64, i32, i32, p, p, p],
+        "mlxvs_knn_keys_device": [p, i64, p, i64, i32, i32, ctypes.c_int, i64, p, p],
+        "mlxvs_hamming_keys_device": [p, i64, p, i64, i32, i32, i64, p, p],
+        "mlxvs_merge_keys_device": [p, i32, i64, i32, i32, p, i32, p, p, p],
+        "mlxvs_device_synchronize": [p],
+    }
+    for name, args in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    lib.mlxvs_last_error.restype = ctypes.c_char_p
+    lib.mlxvs_last_error.argtypes = []
+    lib.mlxvs_version.restype = ctypes.c_char_p
+    lib.mlxvs_version.argtypes = []
+    _lib = lib
+    return lib
+
+
+def version():
+    return _load().mlxvs_version().decode()
+
+
+def _check(rc):
+    if rc == 0:
+        return
+    msg = _lib.mlxvs_last_error().decode()
+    if rc == 1:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def _metric(metric):
+    """A Metric from a Metric, its value or its name (python/mlxvs/__init__.py:80-103)."""
+    if isinstance(metric, str):
+        try:
+            return Metric[metric]
+        except KeyError:
+            names = ", ".join(repr(n) for n in Metric.__members__)
+            raise ValueError(f"unknown Metric {metric!r}; one of {names}") from None
+    try:
+        return Metric(int(metric))
+    except (TypeError, ValueError):
+        raise ValueError(f"unknown Metric {metric!r}") from None
+
+
+def _is_torch(x):
+    return type(x).__module__.startswith("torch") and hasattr(x, "is_cuda")
+
+
+def _host_float_rows(x, op, name):
+    """float_rows (src/utils.h:18-29) on host arrays: 2-D, real, as float32."""
+    if _is_torch(x):
+        x = x.detach().cpu().float().numpy() if x.dtype != _torch().bool else x.numpy()
+    a = np.asarray(x)
+    if a.ndim != 2:
+        raise ValueError(f"[{op}] {name} must be 2-D [n, d].")
+    if a.dtype == np.bool_ or np.iscomplexobj(a) or not np.issubdtype(a.dtype, np.number):
+        raise ValueError(f"[{op}] {name} must be real numbers.")
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _dev_float_rows(x, op, name):
+    torch = _torch()
+    if x.dim() != 2:
+        raise ValueError(f"[{op}] {name} must be 2-D [n, d].")
+    if x.dtype == torch.bool or x.is_complex():
+        raise ValueError(f"[{op}] {name} must be real numbers.")
+    return x.to(torch.float32).contiguous()
+
+
+def _stream_handle(stream, device):
+    if stream is None:
+        return ctypes.c_void_p(_torch().cuda.current_stream(device).cuda_stream)
+    if isinstance(stream, int):
+        return ctypes.c_void_p(stream)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def brute_force_knn(base, queries, k, metric=Metric.l2, *, tile_rows=65536, stream=None):
+    """Exact k-nearest neighbors of every query among the base rows.
+
+    Same arguments and results as the reference's mlxvs.brute_force_knn
+    (python/bindings.cpp:37-75).  tile_rows is accepted for compatibility;
+    the kernels choose their own tiling.
+    """
+    op = "mlxvs::brute_force_knn"
+    m = _metric(metric)
+    lib = _load()
+    k = int(k)
+    if _is_torch(base) and _is_torch(queries) and base.is_cuda and queries.is_cuda:
+        torch = _torch()
+        b = _dev_float_rows(base, op, "base")
+        q = _dev_float_rows(queries, op, "queries")
+        if b.shape[1] != q.shape[1]:
+            raise ValueError(f"[{op}] base and queries must have the same number of columns.")
+        if b.device != q.device:
+            raise ValueError(f"[{op}] base and queries must be on the same device.")
+        nq = q.shape[0]
+        ids = torch.empty((nq, max(k, 0)), dtype=torch.int32, device=q.device)
+        dist = torch.empty((nq, max(k, 0)), dtype=torch.float32, device=q.device)
+        with torch.cuda.device(q.device):
+            _check(lib.mlxvs_brute_force_knn_device(
+                b.data_ptr(), b.shape[0], q.data_ptr(), nq, b.shape[1], k, int(m),
+                ids.data_ptr(), dist.data_ptr(), _stream_handle(stream, q.device)))
+        return ids, dist
+    b = _host_float_rows(base, op, "base")
+    q = _host_float_rows(queries, op, "queries")
+    if b.shape[1] != q.shape[1]:
+        raise ValueError(f"[{op}] base and queries must have the same number of columns.")
+    nq = q.shape[0]
+    ids = np.empty((nq, max(k, 0)), np.int32)
+    dist = np.empty((nq, max(k, 0)), np.float32)
+    _check(lib.mlxvs_brute_force_knn(
+        b.ctypes.data, b.shape[0], q.ctypes.data, nq, b.shape[1], k, int(m),
+        ids.ctypes.data, dist.ctypes.data))
+    return ids, dist
+
+
+def _host_codes(x, op, name):
+    if _is_torch(x):
+        x = x.detach().cpu().numpy()
+    a = np.asarray(x)
+    if a.ndim != 2 or a.dtype != np.uint8:
+        raise ValueError(f"[{op}] {name} must be bit-packed uint8 [n, bytes].")
+    return np.ascontiguousarray(a)
+
+
+def hamming_knn(rows, queries, k, *, stream=None):
+    """Exact k-NN by Hamming distance of bit-packed uint8 rows.
+
+    Same arguments and results as the reference's mlxvs.hamming_knn
+    (python/bindings.cpp:681-710): ids int32 [nq, k] and the Hamming
+    distances as float32 [nq, k], nearest first, ties to the lower id.
+    """
+    op = "mlxvs::hamming_knn"
+    lib = _load()
+    k = int(k)
+    if _is_torch(rows) and _is_torch(queries) and rows.is_cuda and queries.is_cuda:
+        torch = _torch()
+        for t, nm in ((rows, "rows"), (queries, "queries")):
+            if t.dim() != 2 or t.dtype != torch.uint8:
+                raise ValueError(f"[{op}] {nm} must be bit-packed uint8 [n, bytes].")
+        if rows.shape[1] != queries.shape[1]:
+            raise ValueError(f"[{op}] queries must have the rows' bytes.")
+        r = rows.contiguous()
+        q = queries.contiguous()
+        nq = q.shape[0]
+        ids = torch.empty((nq, max(k, 0)), dtype=torch.int32, device=q.device)
+        dist = torch.empty((nq, max(k, 0)), dtype=torch.float32, device=q.device)
+        with torch.cuda.device(q.device):
+            _check(lib.mlxvs_hamming_knn_device(
+                r.data_ptr(), r.shape[0], q.data_ptr(), nq, r.shape[1], k,
+                ids.data_ptr(), dist.data_ptr(), _stream_handle(stream, q.device)))
+        return ids, dist
+    r = _host_codes(rows, op, "rows")
+    q = _host_codes(queries, op, "queries")
+    if r.shape[1] != q.shape[1]:
+        raise ValueError(f"[{op}] queries must have the rows' bytes.")
+    nq = q.shape[0]
+    ids = np.empty((nq, max(k, 0)), np.int32)
+    dist = np.empty((nq, max(k, 0)), np.float32)
+    _check(lib.mlxvs_hamming_knn(
+        r.ctypes.data, r.shape[0], q.ctypes.data, nq, r.shape[1], k,
+        ids.ctypes.data, dist.ctypes.data))
+    return ids, dist
+
+
+def knn_keys(base, queries, k, metric=Metric.l2, *, id_offset=0, stream=None):
+    """One shard's k best candidates per query as int64 keys [nq, k] (CUDA tensors).
+
+    A key holds (order_bits(score) << 32) | ~id as a 64-bit pattern (see
+    include/mlxvs_c.h); larger is better, 0 is an empty slot.
+    """
+    op = "mlxvs::brute_force_knn"
+    torch = _torch()
+    lib = _load()
+    m = _metric(metric)
+    b = _dev_float_rows(base, op, "base")
+    q = _dev_float_rows(queries, op, "queries")
+    if b.shape[1] != q.shape[1]:
+        raise ValueError(f"[{op}] base and queries must have the same number of columns.")
+    keys = torch.empty((q.shape[0], k), dtype=torch.int64, device=q.device)
+    with torch.cuda.device(q.device):
+        _check(lib.mlxvs_knn_keys_device(
+            b.data_ptr(), b.shape[0], q.data_ptr(), q.shape[0], b.shape[1], int(k), int(m),
+            int(id_offset), keys.data_ptr(), _stream_handle(stream, q.device)))
+    return keys
+
+
+def hamming_keys(rows, queries, k, *, id_offset=0, stream=None):
+    """One shard's Hamming candidates as int64 keys [nq, k] (CUDA tensors)."""
+    torch = _torch()
+    lib = _load()
+    r = rows.contiguous()
+    q = queries.contiguous()
+    if r.dtype != torch.uint8 or q.dtype != torch.uint8 or r.dim() != 2 or q.dim() != 2:
+        raise ValueError("[mlxvs::hamming_knn] rows must be bit-packed uint8 [n, bytes].")
+    if r.shape[1] != q.shape[1]:
+        raise ValueError("[mlxvs::hamming_knn] queries must have the rows' bytes.")
+    keys = torch.empty((q.shape[0], k), dtype=torch.int64, device=q.device)
+    with torch.cuda.device(q.device):
+        _check(lib.mlxvs_hamming_keys_device(
+            r.data_ptr(), r.shape[0], q.data_ptr(), q.shape[0], r.shape[1], int(k),
+            int(id_offset), keys.data_ptr(), _stream_handle(stream, q.device)))
+    return keys
+
+
+def merge_keys(lists, k, kind, queries=None, *, stream=None):
+    """Best k of key lists [L, nq, k] (a CUDA int64 tensor) as (ids, distances).
+
+    kind: a Metric (or its name) or "hamming".  L2 distances need the queries.
+    """
+    torch = _torch()
+    lib = _load()
+    kind = KIND_HAMMING if kind == "hamming" else int(_metric(kind))
+    lists = lists.contiguous()
+    L, nq, kk = lists.shape
+    if kk != k:
+        raise ValueError("[mlxvs::merge_keys] lists must be [L, nq, k].")
+    ids = torch.empty((nq, k), dtype=torch.int32, device=lists.device)
+    dist = torch.empty((nq, k), dtype=torch.float32, device=lists.device)
+    qp, d = 0, 0
+    if queries is not None:
+        q = queries.to(torch.float32).contiguous()
+        qp, d = q.data_ptr(), q.shape[1]
+    with torch.cuda.device(lists.device):
+        _check(lib.mlxvs_merge_keys_device(
+            lists.data_ptr(), L, nq, int(k), kind, qp, d, ids.data_ptr(), dist.data_ptr(),
+            _stream_handle(stream, lists.device)))
+    return ids, dist
+
+
+def synchronize(stream=None, device=None):
+    """Waits for the stream and raises if a kernel recorded an error."""
+    torch = _torch()
+    dev = device if device is not None else torch.cuda.current_device()
+    with torch.cuda.device(dev):
+        _check(_load().mlxvs_device_synchronize(_stream_handle(stream, dev)))

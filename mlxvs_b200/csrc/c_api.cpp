@@ -1,0 +1,224 @@
+// The C API (include/mlxvs_c.h) over the engine.  Error handling restates
+// the reference's: std::invalid_argument -> MLXVS_ERROR_INVALID_ARGUMENT, any
+// other exception -> MLXVS_ERROR_INTERNAL, the message kept per thread and
+// cleared on success (ref: src/c_api.cpp:28-47).
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "engine.h"
+#include "mlxvs_c.h"
+
+namespace {
+
+thread_local std::string last_error;
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    last_error.clear();
+    return MLXVS_OK;
+  } catch (const std::invalid_argument& e) {
+    last_error = e.what();
+    return MLXVS_ERROR_INVALID_ARGUMENT;
+  } catch (const std::exception& e) {
+    last_error = e.what();
+    return MLXVS_ERROR_INTERNAL;
+  } catch (...) {
+    last_error = "unknown error";
+    return MLXVS_ERROR_INTERNAL;
+  }
+}
+
+void require(bool ok, const char* what) {
+  if (!ok) throw std::invalid_argument(std::string("[mlxvs] ") + what);
+}
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string("[mlxvs_b200] CUDA error: ") + cudaGetErrorString(e) +
+                             " (" + what + ")");
+  }
+}
+
+mlxvs_b200::Metric to_metric(mlxvs_metric m) {
+  switch (m) {
+    case MLXVS_INNER_PRODUCT:
+      return mlxvs_b200::Metric::InnerProduct;
+    case MLXVS_L2:
+      return mlxvs_b200::Metric::L2;
+    case MLXVS_COSINE:
+      return mlxvs_b200::Metric::Cosine;
+  }
+  throw std::invalid_argument("[mlxvs] unknown metric.");
+}
+
+// ref: host_rows, src/c_api.cpp:84-91
+void host_rows(const void* rows, int64_t n, int32_t d) {
+  require(rows != nullptr || n == 0, "rows must not be NULL.");
+  require(n >= 0 && n < (1LL << 31), "the number of rows must be in [0, 2^31).");
+  require(d >= 1, "the dimension must be at least 1.");
+}
+
+// Device buffers of one host-memory call, freed in stream order.
+struct DeviceBuffers {
+  cudaStream_t s = nullptr;
+  void* ptrs[8] = {};
+  int count = 0;
+  explicit DeviceBuffers(cudaStream_t st) : s(st) {}
+  void* alloc(size_t bytes) {
+    void* p = nullptr;
+    ck(cudaMallocAsync(&p, bytes > 0 ? bytes : 256, s), "cudaMallocAsync");
+    ptrs[count++] = p;
+    return p;
+  }
+  ~DeviceBuffers() {
+    for (int i = 0; i < count; ++i) cudaFreeAsync(ptrs[i], s);
+  }
+};
+
+// One non-blocking stream per host thread for the host-memory entry points.
+cudaStream_t thread_stream() {
+  thread_local cudaStream_t s = nullptr;
+  thread_local int dev = -1;
+  int cur = 0;
+  ck(cudaGetDevice(&cur), "cudaGetDevice");
+  if (s == nullptr || dev != cur) {
+    ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+    dev = cur;
+  }
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mlxvs_last_error(void) { return last_error.c_str(); }
+
+const char* mlxvs_version(void) { return mlxvs_b200::version(); }
+
+int mlxvs_brute_force_knn(const float* base, int64_t n, const float* queries, int64_t nq,
+                          int32_t d, int32_t k, mlxvs_metric metric, int32_t* ids,
+                          float* distances) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(base, n, d);
+    host_rows(queries, nq, d);
+    mlxvs_b200::Metric m = to_metric(metric);
+    require(k >= 1 && k <= 256, "k must be in [1, 256].");
+    if (nq == 0) return;
+    cudaStream_t s = thread_stream();
+    DeviceBuffers buf(s);
+    const size_t bbytes = (size_t)n * d * sizeof(float);
+    const size_t qbytes = (size_t)nq * d * sizeof(float);
+    const size_t count = (size_t)nq * k;
+    float* db = static_cast<float*>(buf.alloc(bbytes));
+    float* dq = static_cast<float*>(buf.alloc(qbytes));
+    int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
+    float* ddist = distances ? static_cast<float*>(buf.alloc(count * sizeof(float))) : nullptr;
+    if (bbytes) ck(cudaMemcpyAsync(db, base, bbytes, cudaMemcpyHostToDevice, s), "copy base");
+    ck(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, s), "copy queries");
+    mlxvs_b200::brute_force_knn(db, n, dq, nq, d, k, m, dids, ddist, s);
+    ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
+    if (distances)
+      ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),
+         "copy distances");
+    mlxvs_b200::device_synchronize(s);
+  });
+}
+
+int mlxvs_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
+                      int32_t bytes, int32_t k, int32_t* ids, float* distances) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(rows, n, bytes);
+    host_rows(queries, nq, bytes);
+    require(k >= 1 && k <= 256, "k must be in [1, 256].");
+    if (nq == 0) return;
+    cudaStream_t s = thread_stream();
+    DeviceBuffers buf(s);
+    const size_t rbytes = (size_t)n * bytes;
+    const size_t qbytes = (size_t)nq * bytes;
+    const size_t count = (size_t)nq * k;
+    uint8_t* dr = static_cast<uint8_t*>(buf.alloc(rbytes));
+    uint8_t* dq = static_cast<uint8_t*>(buf.alloc(qbytes));
+    int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
+    float* ddist = distances ? static_cast<float*>(buf.alloc(count * sizeof(float))) : nullptr;
+    if (rbytes) ck(cudaMemcpyAsync(dr, rows, rbytes, cudaMemcpyHostToDevice, s), "copy rows");
+    ck(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, s), "copy queries");
+    mlxvs_b200::hamming_knn(dr, n, dq, nq, bytes, k, dids, ddist, s);
+    ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
+    if (distances)
+      ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),
+         "copy distances");
+    mlxvs_b200::device_synchronize(s);
+  });
+}
+
+int mlxvs_brute_force_knn_device(const float* base, int64_t n, const float* queries, int64_t nq,
+                                 int32_t d, int32_t k, mlxvs_metric metric, int32_t* ids,
+                                 float* distances, void* stream) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(base, n, d);
+    host_rows(queries, nq, d);
+    mlxvs_b200::brute_force_knn(base, n, queries, nq, d, k, to_metric(metric), ids, distances,
+                                static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_hamming_knn_device(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
+                             int32_t bytes, int32_t k, int32_t* ids, float* distances,
+                             void* stream) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(rows, n, bytes);
+    host_rows(queries, nq, bytes);
+    mlxvs_b200::hamming_knn(rows, n, queries, nq, bytes, k, ids, distances,
+                            static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_knn_keys_device(const float* base, int64_t n, const float* queries, int64_t nq,
+                          int32_t d, int32_t k, mlxvs_metric metric, int64_t id_offset,
+                          uint64_t* keys, void* stream) {
+  return guarded([&] {
+    require(keys != nullptr, "keys must not be NULL.");
+    host_rows(base, n, d);
+    host_rows(queries, nq, d);
+    mlxvs_b200::knn_keys(base, n, queries, nq, d, k, to_metric(metric), id_offset, keys,
+                         static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_hamming_keys_device(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
+                              int32_t bytes, int32_t k, int64_t id_offset, uint64_t* keys,
+                              void* stream) {
+  return guarded([&] {
+    require(keys != nullptr, "keys must not be NULL.");
+    host_rows(rows, n, bytes);
+    host_rows(queries, nq, bytes);
+    mlxvs_b200::hamming_keys(rows, n, queries, nq, bytes, k, id_offset, keys,
+                             static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_merge_keys_device(const uint64_t* lists, int32_t num_lists, int64_t nq, int32_t k,
+                            int32_t kind, const float* queries, int32_t d, int32_t* ids,
+                            float* distances, void* stream) {
+  return guarded([&] {
+    mlxvs_b200::merge_keys(lists, num_lists, nq, k, kind, queries, d, ids, distances,
+                           static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_device_synchronize(void* stream) {
+  return guarded([&] { mlxvs_b200::device_synchronize(static_cast<cudaStream_t>(stream)); });
+}
+
+}  // extern "C"

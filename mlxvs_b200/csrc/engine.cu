@@ -1,0 +1,553 @@
+// Host side of the exact k-NN engine: argument checks, scratch memory from
+// the stream-ordered pool, TMA tensor maps, the choice between the exact
+// one-pass fp16 path and the split-fp16 path, work decomposition and launches.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "gemm_topk.cuh"
+#include "hamming.cuh"
+#include "knn_kernels.cuh"
+
+#ifndef MLXVS_B200_VERSION
+#define MLXVS_B200_VERSION "0.16.1-b200"
+#endif
+
+namespace mlxvs_b200 {
+
+namespace {
+
+// Bounded waits inside the kernels give up after this long (no legitimate
+// wait comes near it: stages turn over in microseconds).
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string("[mlxvs_b200] CUDA error: ") + cudaGetErrorString(e) +
+                             " (" + what + ")");
+  }
+}
+#define CK(x) check_cuda((x), #x)
+
+void require(bool ok, const std::string& msg) {
+  if (!ok) throw std::invalid_argument(msg);
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem = 0;
+  uint32_t* err = nullptr;  // error word of the kernels' bounded waits
+};
+
+DeviceInfo& device_info() {
+  static std::mutex mu;
+  static DeviceInfo infos[64];
+  static bool ready[64] = {};
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> guard(mu);
+  DeviceInfo& info = infos[dev];
+  if (!ready[dev]) {
+    int major = 0, minor = 0;
+    CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      throw std::runtime_error("[mlxvs_b200] needs an sm_100 GPU (B200); device " +
+                               std::to_string(dev) + " is sm_" + std::to_string(major) +
+                               std::to_string(minor));
+    CK(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaDeviceGetAttribute(&info.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    CK(cudaMalloc(&info.err, 16));
+    CK(cudaMemset(info.err, 0, 16));
+    // keep freed scratch in this process's pool between calls
+    cudaMemPool_t pool;
+    CK(cudaDeviceGetDefaultMemPool(&pool, dev));
+    uint64_t keep = UINT64_MAX;
+    CK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    ready[dev] = true;
+  }
+  return info;
+}
+
+// Scratch buffers of one call, returned to the pool in stream order.
+struct Scratch {
+  cudaStream_t s;
+  std::vector<void*> ptrs;
+  explicit Scratch(cudaStream_t st) : s(st) {}
+  template <class T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    CK(cudaMallocAsync(&p, std::max<size_t>(count * sizeof(T), 256), s));
+    ptrs.push_back(p);
+    return static_cast<T*>(p);
+  }
+  ~Scratch() {
+    for (void* p : ptrs) cudaFreeAsync(p, s);
+  }
+};
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) throw std::runtime_error("[mlxvs_b200] cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// 2-D fp16 tensor [rows, cols] (cols contiguous), tiles of box_cols x
+// box_rows written to shared memory with the 128-byte swizzle.
+CUtensorMap map_f16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                    uint32_t box_rows) {
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("[mlxvs_b200] cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return m;
+}
+
+// Base ranges per query block: the fewest waves of units over the slots,
+// each unit paying a fixed start cost of about `overhead` tiles.
+int choose_splits(int qblocks, int tiles, int slots, double overhead, int max_splits) {
+  int best = 1;
+  double best_cost = 1e300;
+  int limit = std::max(1, std::min(tiles, max_splits));
+  for (int s = 1; s <= limit; ++s) {
+    int64_t units = (int64_t)qblocks * s;
+    int64_t waves = (units + slots - 1) / slots;
+    double per_unit = std::ceil((double)tiles / s) + overhead;
+    double cost = (double)waves * per_unit;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
+  if (p.n_pad == 0) return;
+  const int threads = 256;
+  int64_t blocks = std::min<int64_t>((p.n_pad + 7) / 8, (int64_t)sms * 16);
+  bool vec = p.lo == nullptr && !p.cosine && p.d % 4 == 0 &&
+             (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+  if (vec)
+    prep_rows_vec4_kernel<<<(unsigned)blocks, threads, 0, s>>>(p);
+  else
+    prep_rows_kernel<<<(unsigned)blocks, threads, 0, s>>>(p);
+  CK(cudaGetLastError());
+}
+
+void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64_t nq, int k,
+                  int kind, const float* qq, uint64_t* out_keys, int32_t* ids, float* dist,
+                  cudaStream_t s) {
+  if (nq == 0) return;
+  int64_t total = (int64_t)num_lists * k;
+  int cap = 2;
+  while (cap < total && cap < MERGE_CAP) cap <<= 1;
+  while (cap <= k) cap <<= 1;
+  merge_keys_kernel<<<(unsigned)nq, MERGE_THREADS, (size_t)cap * 8, s>>>(
+      lists, num_lists, list_rows, nq, k, kind, qq, out_keys, ids, dist, cap);
+  CK(cudaGetLastError());
+}
+
+void launch_fill(int64_t count, int kind, int32_t* ids, float* dist, uint64_t* keys,
+                 cudaStream_t s) {
+  if (count == 0) return;
+  unsigned blocks = (unsigned)std::min<int64_t>((count + 255) / 256, 4096);
+  fill_missing_kernel<<<blocks, 256, 0, s>>>(count, kind, ids, dist, keys);
+  CK(cudaGetLastError());
+}
+
+template <int QB, int NPASS>
+void launch_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                 const CUtensorMap& b_lo, const KnnGemmParams& p, int grid, uint32_t smem,
+                 cudaStream_t s) {
+  auto kern = knn_gemm_topk_kernel<QB, NPASS>;
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<grid, GemmLayout<QB, NPASS>::THREADS, smem, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+  CK(cudaGetLastError());
+}
+
+void check_rows(int64_t n, const char* what) {
+  require(n >= 0 && n < (1LL << 31),
+          std::string("[mlxvs::brute_force_knn] the number of ") + what +
+              " must be in [0, 2^31).");
+}
+
+// The exact k-NN of queries among base: keys [nq, k] (out_keys) and / or ids
+// and distances.  The per-call flow:
+//   1. prep: fp32 -> fp16 operand rows (2q for L2), |b|^2, |q|^2, and whether
+//      every value is exactly an fp16 (one host sync to read the flags);
+//   2. if not: split-fp16 operands hi / lo with power-of-two scales;
+//   3. the fused GEMM + top-k kernel over (query block, base range) units;
+//   4. merge of the units' lists into the k best, then distances.
+void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+              Metric metric, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
+              cudaStream_t s) {
+  require(k >= 1 && k <= 256, "[mlxvs::brute_force_knn] k must be in [1, 256].");
+  require(d >= 1, "[mlxvs::brute_force_knn] the dimension must be at least 1.");
+  check_rows(n, "base rows");
+  check_rows(nq, "queries");
+  const int mi = static_cast<int>(metric);
+  require(mi >= 0 && mi <= 2, "[mlxvs::brute_force_knn] unknown metric.");
+  require(id_offset >= 0 && id_offset + n <= (1LL << 31),
+          "[mlxvs::brute_force_knn] ids must fit in int32.");
+  DeviceInfo& dev = device_info();
+  if (nq == 0) return;
+  if (n == 0) {
+    launch_fill(nq * k, mi, ids, dist, out_keys, s);
+    return;
+  }
+  require(base != nullptr && queries != nullptr, "[mlxvs::brute_force_knn] null input.");
+  const bool l2 = metric == Metric::L2;
+  const bool cosine = metric == Metric::Cosine;
+  const int d_pad = (int)round_up(d, GT_KCH);
+  const int kchunks = d_pad / GT_KCH;
+  const int64_t n_pad = round_up(n, GT_BN);
+  const int64_t nq_pad = round_up(nq, 128);
+
+  Scratch sc(s);
+  __half* b_hi = sc.alloc<__half>((size_t)n_pad * d_pad);
+  __half* q_hi = sc.alloc<__half>((size_t)nq_pad * d_pad);
+  float* nb = sc.alloc<float>((size_t)n_pad);
+  float* qq = l2 ? sc.alloc<float>((size_t)nq_pad) : nullptr;
+  uint32_t* flags = sc.alloc<uint32_t>(4);
+  CK(cudaMemsetAsync(flags, 0, 16, s));
+
+  PrepParams pb{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, 1.0f, b_hi, nullptr,
+                nb, l2 ? 1.0f : 0.0f, INFINITY, flags};
+  PrepParams pq{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, 1.0f, q_hi,
+                nullptr, qq, 1.0f, 0.0f, flags + 2};
+  launch_prep(pb, dev.sms, s);
+  launch_prep(pq, dev.sms, s);
+  uint32_t hflags[4];
+  CK(cudaMemcpyAsync(hflags, flags, 16, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  const bool exact = hflags[0] == 0 && hflags[2] == 0;
+
+  __half* b_lo = nullptr;
+  __half* q_lo = nullptr;
+  float out_scale = 1.0f;
+  if (!exact) {
+    float amax_b, amax_q;
+    std::memcpy(&amax_b, &hflags[1], 4);
+    std::memcpy(&amax_q, &hflags[3], 4);
+    // power-of-two scales putting each operand's largest |value| in
+    // [2^14, 2^15): the fp16 hi part keeps 11 bits, lo the next 11
+    auto scale_exp = [](float amax) {
+      if (!(amax > 0.0f) || !std::isfinite(amax)) return 0;
+      return std::max(-60, std::min(60, 14 - std::ilogb(amax)));
+    };
+    const int eb = scale_exp(amax_b), eq = scale_exp(amax_q);
+    const float sb = std::ldexp(1.0f, eb), sq = std::ldexp(1.0f, eq);
+    b_lo = sc.alloc<__half>((size_t)n_pad * d_pad);
+    q_lo = sc.alloc<__half>((size_t)nq_pad * d_pad);
+    PrepParams pb2{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, b_lo,
+                   nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr};
+    PrepParams pq2{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, sq, q_hi,
+                   q_lo, nullptr, 0.0f, 0.0f, nullptr};
+    launch_prep(pb2, dev.sms, s);
+    launch_prep(pq2, dev.sms, s);
+    out_scale = std::ldexp(1.0f, -(eb + eq));
+  }
+
+  // kernel shape: 128 queries per CTA when the heaps fit (64, 32 or 16 for
+  // large k: the MMA still computes 128 rows, the rest of the lanes are unused),
+  // the query block resident in shared memory when it fits with >= 3 stages
+  const int npa = exact ? 1 : 2;
+  const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
+  int QB = 0, stages = 0, a_stream = 0;
+  for (int pass = 0; pass < 3 && QB == 0; ++pass) {
+    const int min_stages = pass < 2 ? 3 : 2;
+    for (int qb : {128, 64, 32, 16}) {
+      if (pass == 0 && qb != 128) continue;  // first try 128 only
+      for (int as : {0, 1}) {
+        for (int st = 8; st >= min_stages; --st) {
+          GemmSmem lay = gemm_smem(qb, npa, kchunks, st, as, k);
+          if (lay.total <= budget) {
+            QB = qb;
+            stages = st;
+            a_stream = as;
+            break;
+          }
+        }
+        if (QB) break;
+      }
+      if (QB) break;
+    }
+  }
+  if (QB == 0) throw std::runtime_error("[mlxvs_b200] no kernel shape fits shared memory");
+  const int qblocks = (int)((nq + QB - 1) / QB);
+  const int tiles = (int)(n_pad / GT_BN);
+  const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
+  const int units = qblocks * splits;
+
+  uint64_t* partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
+  unsigned long long* gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
+  CK(cudaMemsetAsync(gfloor, 0, (size_t)nq_pad * 8, s));
+
+  CUtensorMap ta_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, QB);
+  CUtensorMap ta_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, QB);
+  CUtensorMap tb_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  CUtensorMap tb_lo = map_f16(b_lo ? b_lo : b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+
+  KnnGemmParams p{};
+  p.qblocks = qblocks;
+  p.tiles = tiles;
+  p.splits = splits;
+  p.units = units;
+  p.kchunks = kchunks;
+  p.k = k;
+  p.stages = stages;
+  p.a_stream = a_stream;
+  p.n_valid = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.id_offset = id_offset;
+  p.nb = nb;
+  p.partial = partial;
+  p.gfloor = gfloor;
+  p.out_scale = out_scale;
+  p.err = dev.err;
+  p.wait_ns = WAIT_LIMIT_NS;
+  const GemmSmem lay = gemm_smem(QB, npa, kchunks, stages, a_stream, k);
+  const uint32_t smem = lay.total + 1024u;
+  const int grid = std::min(units, dev.sms);
+  if (QB == 128) {
+    if (exact)
+      launch_gemm<128, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+    else
+      launch_gemm<128, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+  } else if (QB == 64) {
+    if (exact)
+      launch_gemm<64, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+    else
+      launch_gemm<64, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+  } else if (QB == 32) {
+    if (exact)
+      launch_gemm<32, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+    else
+      launch_gemm<32, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+  } else {
+    if (exact)
+      launch_gemm<16, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+    else
+      launch_gemm<16, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+  }
+  launch_merge(partial, splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s);
+}
+
+// ------------------------------------------------------------------ Hamming
+
+struct HammingOut {
+  uint64_t* keys;
+  int32_t* ids;
+  float* dist;
+};
+
+// Picks the ring depth and split count of one kernel shape from its
+// occupancy, then launches the scan and the merge of its lists.
+template <int V, int QH>
+void launch_hamming_t(HammingParams p, const DeviceInfo& dev, Scratch& sc, const HammingOut& out,
+                      cudaStream_t s) {
+  auto kern = hamming_topk_kernel<V, QH>;
+  int stages = 4;
+  uint32_t smem = hamming_smem_bytes(V, QH, p.k, stages);
+  while (smem > (uint32_t)dev.max_smem && stages > 2)
+    smem = hamming_smem_bytes(V, QH, p.k, --stages);
+  if (smem > (uint32_t)dev.max_smem)
+    throw std::runtime_error("[mlxvs_b200] hamming: no kernel shape fits shared memory");
+  p.stages = stages;
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 1;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, QH + 32, smem));
+  const int slots = dev.sms * std::max(per_sm, 1);
+  p.splits = choose_splits(p.qblocks, p.tiles, slots, 2.0, 64);
+  p.units = p.qblocks * p.splits;
+  p.partial = sc.alloc<uint64_t>((size_t)p.splits * p.nq_pad * p.k);
+  const int grid = std::min(p.units, slots);
+  kern<<<grid, QH + 32, smem, s>>>(p);
+  CK(cudaGetLastError());
+  launch_merge(p.partial, p.splits, p.nq_pad, p.nq, p.k, KIND_HAMMING, nullptr, out.keys, out.ids,
+               out.dist, s);
+}
+
+template <int V>
+void launch_hamming_v(const HammingParams& p, int QH, const DeviceInfo& dev, Scratch& sc,
+                      const HammingOut& out, cudaStream_t s) {
+  if constexpr (V <= 16) {
+    if (QH == 256) return launch_hamming_t<V, 256>(p, dev, sc, out, s);
+  }
+  if (QH == 128) return launch_hamming_t<V, 128>(p, dev, sc, out, s);
+  return launch_hamming_t<V, 64>(p, dev, sc, out, s);
+}
+
+void hamming_core(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                  int k, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
+                  cudaStream_t s) {
+  require(k >= 1 && k <= 256, "[mlxvs::hamming_knn] k must be in [1, 256].");
+  require(bytes >= 1, "[mlxvs::hamming_knn] rows must be bit-packed uint8 [n, bytes].");
+  require(bytes <= 512, "[mlxvs::hamming_knn] codes longer than 4096 bits are not supported.");
+  require(n >= 0 && n < (1LL << 31),
+          "[mlxvs::hamming_knn] the number of rows must be in [0, 2^31).");
+  require(nq >= 0 && nq < (1LL << 31),
+          "[mlxvs::hamming_knn] the number of queries must be in [0, 2^31).");
+  require(id_offset >= 0 && id_offset + n <= (1LL << 31),
+          "[mlxvs::hamming_knn] ids must fit in int32.");
+  DeviceInfo& dev = device_info();
+  if (nq == 0) return;
+  if (n == 0) {
+    launch_fill(nq * k, KIND_HAMMING, ids, dist, out_keys, s);
+    return;
+  }
+  require(rows != nullptr && queries != nullptr, "[mlxvs::hamming_knn] null input.");
+  int V = 1;
+  while (V * 16 < bytes) V <<= 1;
+  const int row_bytes = 16 * V;
+  Scratch sc(s);
+  const uint8_t* r = rows;
+  const uint8_t* qv = queries;
+  // codes zero padded to 16 V bytes (zeros XOR zeros add nothing) when the
+  // caller's layout is not already that, or not 16-byte aligned
+  if (row_bytes != bytes || (reinterpret_cast<uintptr_t>(rows) & 15)) {
+    uint8_t* pr = sc.alloc<uint8_t>((size_t)n * row_bytes);
+    CK(cudaMemsetAsync(pr, 0, (size_t)n * row_bytes, s));
+    CK(cudaMemcpy2DAsync(pr, row_bytes, rows, bytes, bytes, n, cudaMemcpyDeviceToDevice, s));
+    r = pr;
+  }
+  if (row_bytes != bytes || (reinterpret_cast<uintptr_t>(queries) & 15)) {
+    uint8_t* pq = sc.alloc<uint8_t>((size_t)nq * row_bytes);
+    CK(cudaMemsetAsync(pq, 0, (size_t)nq * row_bytes, s));
+    CK(cudaMemcpy2DAsync(pq, row_bytes, queries, bytes, bytes, nq, cudaMemcpyDeviceToDevice, s));
+    qv = pq;
+  }
+  // queries per CTA: 256 while the heaps stay within 64 KB (two CTAs per SM)
+  int QH = 256;
+  while (QH > 64 && (uint32_t)QH * k * 8u > 64u * 1024u) QH >>= 1;
+  if (V > 16 && QH > 128) QH = 128;
+  const int64_t nq_pad = round_up(nq, QH);
+  HammingParams p{};
+  p.rows = r;
+  p.queries = qv;
+  p.n = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.qblocks = (int)(nq_pad / QH);
+  p.tiles = (int)((n + HM_HT - 1) / HM_HT);
+  p.k = k;
+  p.id_offset = id_offset;
+  p.err = dev.err;
+  p.wait_ns = WAIT_LIMIT_NS;
+  p.gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
+  CK(cudaMemsetAsync(p.gfloor, 0, (size_t)nq_pad * 8, s));
+  const HammingOut out{out_keys, ids, dist};
+  switch (V) {
+    case 1: return launch_hamming_v<1>(p, QH, dev, sc, out, s);
+    case 2: return launch_hamming_v<2>(p, QH, dev, sc, out, s);
+    case 4: return launch_hamming_v<4>(p, QH, dev, sc, out, s);
+    case 8: return launch_hamming_v<8>(p, QH, dev, sc, out, s);
+    case 16: return launch_hamming_v<16>(p, QH, dev, sc, out, s);
+    default: return launch_hamming_v<32>(p, QH, dev, sc, out, s);
+  }
+}
+
+}  // namespace
+
+void brute_force_knn(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+                     Metric metric, int32_t* ids, float* dist, cudaStream_t s,
+                     const KnnOptions& options) {
+  (void)options;
+  require(ids != nullptr || nq == 0, "[mlxvs::brute_force_knn] ids must not be NULL.");
+  knn_core(base, n, queries, nq, d, k, metric, 0, nullptr, ids, dist, s);
+}
+
+void knn_keys(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+              Metric metric, int64_t id_offset, uint64_t* keys, cudaStream_t s) {
+  require(keys != nullptr || nq == 0, "[mlxvs::brute_force_knn] keys must not be NULL.");
+  knn_core(base, n, queries, nq, d, k, metric, id_offset, keys, nullptr, nullptr, s);
+}
+
+void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                 int k, int32_t* ids, float* dist, cudaStream_t s) {
+  require(ids != nullptr || nq == 0, "[mlxvs::hamming_knn] ids must not be NULL.");
+  hamming_core(rows, n, queries, nq, bytes, k, 0, nullptr, ids, dist, s);
+}
+
+void hamming_keys(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                  int k, int64_t id_offset, uint64_t* keys, cudaStream_t s) {
+  require(keys != nullptr || nq == 0, "[mlxvs::hamming_knn] keys must not be NULL.");
+  hamming_core(rows, n, queries, nq, bytes, k, id_offset, keys, nullptr, nullptr, s);
+}
+
+void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kind,
+                const float* queries, int d, int32_t* ids, float* dist, cudaStream_t s) {
+  require(k >= 1 && k <= 256, "[mlxvs::merge_keys] k must be in [1, 256].");
+  require(num_lists >= 0, "[mlxvs::merge_keys] num_lists must be >= 0.");
+  require(nq >= 0 && nq < (1LL << 31), "[mlxvs::merge_keys] nq must be in [0, 2^31).");
+  require(kind >= 0 && kind <= KIND_HAMMING, "[mlxvs::merge_keys] unknown kind.");
+  require(ids != nullptr || nq == 0, "[mlxvs::merge_keys] ids must not be NULL.");
+  DeviceInfo& dev = device_info();
+  if (nq == 0) return;
+  require(lists != nullptr || num_lists == 0, "[mlxvs::merge_keys] lists must not be NULL.");
+  Scratch sc(s);
+  float* qq = nullptr;
+  if (kind == static_cast<int>(Metric::L2)) {
+    require(queries != nullptr && d >= 1,
+            "[mlxvs::merge_keys] L2 distances need the queries [nq, d].");
+    qq = sc.alloc<float>((size_t)nq);
+    unsigned blocks = (unsigned)std::min<int64_t>((nq + 7) / 8, (int64_t)dev.sms * 16);
+    row_sumsq_kernel<<<blocks, 256, 0, s>>>(queries, nq, d, qq);
+    CK(cudaGetLastError());
+  }
+  if (num_lists == 0) {
+    launch_fill(nq * k, kind, ids, dist, nullptr, s);
+    return;
+  }
+  launch_merge(lists, num_lists, nq, nq, k, kind, qq, nullptr, ids, dist, s);
+}
+
+void device_synchronize(cudaStream_t s) {
+  DeviceInfo& dev = device_info();
+  CK(cudaStreamSynchronize(s));
+  uint32_t err = 0;
+  CK(cudaMemcpy(&err, dev.err, 4, cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    CK(cudaMemset(dev.err, 0, 4));
+    throw std::runtime_error("[mlxvs_b200] a kernel gave up waiting (error word " +
+                             std::to_string(err) + ")");
+  }
+}
+
+const char* version() { return MLXVS_B200_VERSION; }
+
+}  // namespace mlxvs_b200

@@ -1,0 +1,54 @@
+// Internal C++ API of the exact k-NN engine (device pointers, stream
+// ordered).  Mirrors the reference's C++ entry points
+// (include/mlxvs/mlxvs.h:22-65, :780-784) with mx::array replaced by device
+// pointers and sizes.  Errors: std::invalid_argument for bad arguments,
+// std::runtime_error for CUDA failures.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mlxvs_b200 {
+
+/** ref: include/mlxvs/mlxvs.h:22-29 */
+enum class Metric : int { InnerProduct = 0, L2 = 1, Cosine = 2 };
+
+/** The kind of a key list: a Metric, or Hamming distances. */
+constexpr int KIND_HAMMING = 3;
+
+/** ref: include/mlxvs/mlxvs.h:45-51.  tile_rows is accepted for signature
+ * compatibility; the kernels pick their own tiles. */
+struct KnnOptions {
+  int tile_rows = 65536;
+};
+
+/** Exact k-NN: ids int32 [nq, k] and distances float32 [nq, k] (dist may be
+ * null).  ref: brute_force_knn, src/knn.cpp:71-142. */
+void brute_force_knn(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+                     Metric metric, int32_t* ids, float* dist, cudaStream_t s,
+                     const KnnOptions& options = {});
+
+/** One shard's k best keys per query [nq, k], best first, ids offset. */
+void knn_keys(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+              Metric metric, int64_t id_offset, uint64_t* keys, cudaStream_t s);
+
+/** Exact Hamming k-NN.  ref: hamming_knn, src/ivf.cpp:1343-1403. */
+void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                 int k, int32_t* ids, float* dist, cudaStream_t s);
+
+void hamming_keys(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                  int k, int64_t id_offset, uint64_t* keys, cudaStream_t s);
+
+/** Best k of num_lists key lists [num_lists][nq][k], as ids and distances
+ * of the given kind (a Metric value or KIND_HAMMING). */
+void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kind,
+                const float* queries, int d, int32_t* ids, float* dist, cudaStream_t s);
+
+/** Waits for s, then throws if a kernel of this library recorded an error
+ * on the current device (and clears it). */
+void device_synchronize(cudaStream_t s);
+
+/** Version string. */
+const char* version();
+
+}  // namespace mlxvs_b200

@@ -1,0 +1,139 @@
+"""ctypes front end of the CPU oracle (oracle.c).
+
+TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference leg use it as the checker or the CPU baseline.
+Nothing in the mlxvs_b200 package imports this module.
+
+The functions mirror the reference's Python API shape
+(python/mlxvs/__init__.py:106-115): numpy in, (ids int32 [nq,k],
+distances float32 [nq,k]) out.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+IP, L2, COSINE = 0, 1, 2
+_METRICS = {"inner_product": IP, "l2": L2, "cosine": COSINE}
+
+
+def build():
+    """Compiles liboracle.so with the committed Makefile."""
+    env = dict(os.environ)
+    subprocess.run(["make", "-s", "-C", _HERE], check=True, env=env)
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        build()
+    lib = ctypes.CDLL(_LIB_PATH)
+    i64, i32, p = ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p
+    lib.oracle_brute_force_knn.argtypes = [p, i64, p, i64, i32, i32, i32, p, p, i32]
+    lib.oracle_brute_force_knn.restype = ctypes.c_int
+    lib.oracle_hamming_knn.argtypes = [p, i64, p, i64, i32, i32, p, p, i32]
+    lib.oracle_hamming_knn.restype = ctypes.c_int
+    lib.oracle_knn_keys.argtypes = [p, i64, p, i64, i32, i32, i32, i64, p, i32]
+    lib.oracle_knn_keys.restype = ctypes.c_int
+    lib.oracle_merge_keys.argtypes = [p, i32, i64, i32, p]
+    lib.oracle_merge_keys.restype = None
+    lib.oracle_key.argtypes = [ctypes.c_float, i32]
+    lib.oracle_key.restype = ctypes.c_uint64
+    _lib = lib
+    return lib
+
+
+def metric_code(metric):
+    if isinstance(metric, str):
+        return _METRICS[metric]
+    return int(metric)
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def brute_force_knn(base, queries, k, metric="l2", threads=0):
+    """Exact k-NN (src/knn.cpp:71-142) on the CPU, float32 math."""
+    lib = _load()
+    base = np.ascontiguousarray(base, dtype=np.float32)
+    queries = np.ascontiguousarray(queries, dtype=np.float32)
+    n, d = base.shape
+    nq = queries.shape[0]
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.float32)
+    rc = lib.oracle_brute_force_knn(
+        _ptr(base), n, _ptr(queries), nq, d, k, metric_code(metric),
+        _ptr(ids), _ptr(dist), threads)
+    if rc != 0:
+        raise ValueError("oracle: invalid argument")
+    return ids, dist
+
+
+def knn_keys(base, queries, k, metric="l2", id_offset=0, threads=0):
+    """The k best 64-bit (score, id) keys per query, best first."""
+    lib = _load()
+    base = np.ascontiguousarray(base, dtype=np.float32)
+    queries = np.ascontiguousarray(queries, dtype=np.float32)
+    n, d = base.shape
+    nq = queries.shape[0]
+    keys = np.empty((nq, k), np.uint64)
+    rc = lib.oracle_knn_keys(
+        _ptr(base), n, _ptr(queries), nq, d, k, metric_code(metric),
+        id_offset, _ptr(keys), threads)
+    if rc != 0:
+        raise ValueError("oracle: invalid argument")
+    return keys
+
+
+def hamming_knn(rows, queries, k, threads=0):
+    """Exact Hamming k-NN of bit-packed uint8 rows (src/ivf.cpp:1343-1403)."""
+    lib = _load()
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    queries = np.ascontiguousarray(queries, dtype=np.uint8)
+    n, nbytes = rows.shape
+    nq = queries.shape[0]
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.float32)
+    rc = lib.oracle_hamming_knn(
+        _ptr(rows), n, _ptr(queries), nq, nbytes, k, _ptr(ids), _ptr(dist), threads)
+    if rc != 0:
+        raise ValueError("oracle: invalid argument")
+    return ids, dist
+
+
+def merge_keys(lists, k):
+    """Best k of L key lists laid out [L, nq, k] (0 = empty slot)."""
+    lib = _load()
+    lists = np.ascontiguousarray(lists, dtype=np.uint64)
+    L, nq, kk = lists.shape
+    assert kk == k
+    out = np.empty((nq, k), np.uint64)
+    lib.oracle_merge_keys(_ptr(lists), L, nq, k, _ptr(out))
+    return out
+
+
+def key(score, idx):
+    return int(_load().oracle_key(float(score), int(idx)))
+
+
+def decode_keys(keys):
+    """(ids int32, scores float32) of 64-bit keys; 0 decodes to (-1, -inf)."""
+    keys = np.asarray(keys, dtype=np.uint64)
+    lo = (keys & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    hi = (keys >> np.uint64(32)).astype(np.uint32)
+    ids = (~lo).view(np.int32).copy()
+    u = np.where(hi & np.uint32(0x80000000), hi ^ np.uint32(0x80000000), ~hi)
+    scores = u.astype(np.uint32).view(np.float32).copy()
+    empty = keys == 0
+    ids[empty] = -1
+    scores[empty] = -np.inf
+    return ids, scores
