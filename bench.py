@@ -1,0 +1,499 @@
+#!/usr/bin/env python
+"""Exact k-NN benchmark (BASELINE.json's metric: queries/s on 1M x 128 fp32,
+L2, k=10, 10k queries; base rows sharded across the GPUs of one node).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+    python bench.py --impl reference ...    (the CPU reference arm)
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+A step is one exact search of every query against the whole base: the
+fp32 -> fp16 input conversion, the fused tcgen05 distance + top-k kernel,
+(for N > 1) the NCCL all-gather of each rank's [nq, k] candidates, and the
+merge to ids and distances.  `value` is whole-job queries/s with the inputs
+resident in HBM (the fp32 base, 512 MB, is larger than L2, so no flush is
+needed); `e2e` is the same through the host-memory API, copies included.
+Inputs are seeded synthetic data with BASELINE's distributions.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # BASELINE config 1 (the headline): 1M x 128 integer-valued fp32, L2
+    "knn-l2-1m-k10": dict(kind="knn", n=1_000_000, nq=10_000, d=128, k=10, metric="l2",
+                          clusters=1024,
+                          desc="exact L2 k-NN, base 1M x 128 fp32 (integer-valued Gaussian "
+                               "mixture, 1024 clusters), 10k queries, k=10"),
+    "knn-l2-1m-k100": dict(kind="knn", n=1_000_000, nq=10_000, d=128, k=100, metric="l2",
+                           clusters=1024, desc="config 1 with k=100"),
+    # BASELINE config 0
+    "knn-l2-100k-k10": dict(kind="knn", n=100_000, nq=1_000, d=128, k=10, metric="l2",
+                            clusters=64, desc="config 0: 100k x 128, 1k queries, k=10"),
+    # BASELINE config 2 (cosine, unit rows with a shared rank-64 part)
+    "knn-cos-1m-1536": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
+                            metric="cosine", rank=64,
+                            desc="config 2: 1M x 1536 fp32 unit rows, cosine, k=10"),
+    # BASELINE config 4
+    "hamming-10m-1024b": dict(kind="hamming", n=10_000_000, nq=10_000, bytes=128, k=10,
+                              prototypes=4096, flip=0.1,
+                              desc="config 4: 10M x 1024-bit codes, 10k queries, k=10"),
+}
+DEFAULT_WORKLOAD = "knn-l2-1m-k10"
+METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pipe roofline"
+
+# DRAM bytes per launch of the dominant kernel, from the committed ncu
+# summaries under profiles/ (None until captured for that workload).
+NCU_TRAFFIC_PER_LAUNCH = {
+    "knn-l2-1m-k10": None,
+}
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm_gbs=p["hbm_gbs"], bf16=p["bf16_tflops"],
+                    bf16_sustained=p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                    source="measured")
+    except (OSError, KeyError, ValueError):
+        return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+# ---------------------------------------------------------------- inputs
+
+def gen_mixture_torch(n, d, clusters, seed, device):
+    """Configs 0/1/3 on the device: centers ~U[0,100]^d, sigma 10, clipped to
+    [0, 255], rounded; float32 (tests/data.py draws the same with NumPy)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    centers = torch.rand((clusters, d), generator=g, device=device) * 100.0
+    out = torch.empty((n, d), dtype=torch.float32, device=device)
+    step = 1 << 20
+    for i in range(0, n, step):
+        m = min(step, n - i)
+        lab = torch.randint(0, clusters, (m,), generator=g, device=device)
+        x = centers[lab] + 10.0 * torch.randn((m, d), generator=g, device=device)
+        out[i:i + m] = x.clamp_(0.0, 255.0).round_()
+    return out
+
+
+def gen_unit_torch(n, d, rank, seed, device):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    basis = torch.randn((rank, d), generator=g, device=device)
+    out = torch.empty((n, d), dtype=torch.float32, device=device)
+    step = 1 << 18
+    for i in range(0, n, step):
+        m = min(step, n - i)
+        x = torch.randn((m, d), generator=g, device=device) + \
+            torch.randn((m, rank), generator=g, device=device) @ basis
+        out[i:i + m] = x / x.norm(dim=1, keepdim=True)
+    return out
+
+
+def gen_codes_torch(n, nbytes, prototypes, flip, seed, device):
+    """Config 4: random prototype codes XOR Bernoulli(flip) bits.  A noise
+    byte b has probability flip^popc(b) (1-flip)^(8-popc(b)): one uniform per
+    byte through that distribution's inverse CDF."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    protos = torch.randint(0, 256, (prototypes, nbytes), generator=g, device=device,
+                           dtype=torch.int32).to(torch.uint8)
+    pc = torch.tensor([bin(b).count("1") for b in range(256)], dtype=torch.float64)
+    cdf = torch.cumsum(flip ** pc * (1.0 - flip) ** (8 - pc), 0)
+    cdf = (cdf / cdf[-1]).to(torch.float32).to(device)
+    out = torch.empty((n, nbytes), dtype=torch.uint8, device=device)
+    step = 1 << 20
+    for i in range(0, n, step):
+        m = min(step, n - i)
+        lab = torch.randint(0, prototypes, (m,), generator=g, device=device)
+        u = torch.rand((m, nbytes), generator=g, device=device)
+        noise = torch.searchsorted(cdf, u).clamp_(max=255).to(torch.uint8)
+        out[i:i + m] = protos[lab] ^ noise
+    return out
+
+
+def make_inputs(w, device, seed=0):
+    if w["kind"] == "knn":
+        base = gen_mixture_torch(w["n"], w["d"], w["clusters"], seed, device)
+        q = gen_mixture_torch(w["nq"], w["d"], w["clusters"], seed + 1, device)
+    elif w["kind"] == "knn-unit":
+        base = gen_unit_torch(w["n"], w["d"], w["rank"], seed, device)
+        q = gen_unit_torch(w["nq"], w["d"], w["rank"], seed + 1, device)
+    else:
+        base = gen_codes_torch(w["n"], w["bytes"], w["prototypes"], w["flip"], seed, device)
+        q = gen_codes_torch(w["nq"], w["bytes"], w["prototypes"], w["flip"], seed + 1, device)
+    return base, q
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append(dict(sm=float(parts[1]), max=float(parts[2]),
+                                     power=float(parts[3]), active=parts[4],
+                                     hw=parts[5], hw_thermal=parts[6], sw_thermal=parts[7],
+                                     sw_power=parts[8]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        max_power = max(r["power"] for r in rows)
+        loaded = [r for r in rows if r["power"] >= 0.5 * max_power] or rows
+        reasons = []
+        for key, name in (("hw", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
+                          ("sw_thermal", "sw_thermal_slowdown"), ("sw_power", "sw_power_cap")):
+            if any(r[key].lower().startswith("active") for r in loaded):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
+                "samples": len(loaded), "power_w_max": max_power}
+
+
+# ---------------------------------------------------------------- CPU side
+
+def cpu_sample_rate(w, base_np, q_np, budget_s, threads=0):
+    """Oracle queries/s on a bounded sample of the workload (all base rows,
+    a subset of the queries), calibrated to take about budget_s seconds."""
+    from oracle import oracle as O
+
+    def run(m):
+        t = time.perf_counter()
+        if w["kind"] == "hamming":
+            O.hamming_knn(base_np, q_np[:m], w["k"], threads=threads)
+        else:
+            O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"], threads=threads)
+        return time.perf_counter() - t
+
+    m = 8
+    t = run(m)
+    while t < 0.5 and m < q_np.shape[0]:
+        m = min(q_np.shape[0], m * 4)
+        t = run(m)
+    rate = m / t
+    m2 = int(min(q_np.shape[0], max(m, rate * budget_s)))
+    t2 = run(m2) if m2 != m else t
+    return m2 / t2, m2, t2
+
+
+def reference_arm(args, w, peaks):
+    """--impl reference: the CPU restatement of the reference's path (the
+    reference itself needs macOS + Metal + MLX) on this host's cores."""
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    import torch
+
+    cores = os.cpu_count() or 1
+    base, q = make_inputs(w, "cpu")
+    base_np, q_np = base.numpy(), q.numpy()
+    # each step: a bounded sample of the workload (all base rows, the first
+    # m queries), m chosen so the whole run stays within a few minutes
+    per_step = max(0.05, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
+    rate, m, _ = cpu_sample_rate(w, base_np, q_np, per_step)
+    from oracle import oracle as O
+
+    def step():
+        if w["kind"] == "hamming":
+            O.hamming_knn(base_np, q_np[:m], w["k"])
+        else:
+            O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"])
+
+    for _ in range(args.warmup):
+        step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t
+    value = m * args.steps / el
+    sample = f"{m} of {w['nq']} queries against all {w['n']} base rows per step"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": w["desc"]},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference (MLX + Metal, macOS only) cannot run here; its CPU "
+                "restatement oracle/oracle.c (OpenMP, all cores) stands in",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of oracle work for cpu_baseline (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    w = WORKLOADS[args.workload]
+    peaks = load_peaks()
+    if args.impl == "reference":
+        return reference_arm(args, w, peaks)
+
+    import torch
+    import torch.distributed as dist
+
+    import mlxvs_b200 as mv
+    from mlxvs_b200 import distributed as mvd
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # inputs: every rank draws the same seeded data and keeps its shard
+    base, q = make_inputs(w, dev)
+    bounds = mvd.shard_bounds(w["n"], world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    shard = base[lo:hi].contiguous()
+    full_base = base
+    k = w["k"]
+    is_hamming = w["kind"] == "hamming"
+    metric = None if is_hamming else w["metric"]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        if world == 1:
+            if is_hamming:
+                return mv.hamming_knn(shard, q, k)
+            return mv.brute_force_knn(shard, q, k, metric)
+        if is_hamming:
+            return mvd.sharded_hamming_knn(shard, q, k, id_offset=lo)
+        return mvd.sharded_brute_force_knn(shard, q, k, metric, id_offset=lo)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    mv.synchronize()
+
+    uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+    gpu_id = f"GPU-{uuid}" if uuid is not None else str(local)
+    sampler = ClockSampler(gpu_id) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    mv.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        ids, dist_out = step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    kname = "hamming_topk" if is_hamming else "gemm_topk"
+    kern_ms, kern_launches = mv.profile_read(kname)
+    _, all_launches = mv.profile_read(None)
+    mv.profile_enable(False)
+    clocks = sampler.stop() if sampler else None
+    mv.synchronize()
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    # a quick self-check of the last step's output on a few queries (rank 0)
+    check = None
+    if rank == 0 and not is_hamming and w["kind"] == "knn":
+        from oracle import oracle as O
+
+        qs = q[:4].cpu().numpy()
+        oids, odist = O.brute_force_knn(full_base.cpu().numpy(), qs, k, metric)
+        check = bool(np.array_equal(ids[:4].cpu().numpy(), oids) and
+                     np.array_equal(dist_out[:4].cpu().numpy(), odist))
+
+    # e2e: the public API on host (pinned) buffers, copies inside the region
+    e2e = None
+    if args.e2e_steps > 0:
+        base_h = shard.cpu().pin_memory()
+        q_h = q.cpu().pin_memory()
+        if world == 1:
+            bnp, qnp = base_h.numpy(), q_h.numpy()
+
+            def e2e_step():
+                if is_hamming:
+                    return mv.hamming_knn(bnp, qnp, k)
+                return mv.brute_force_knn(bnp, qnp, k, metric)
+        else:
+            def e2e_step():
+                sd = base_h.to(dev, non_blocking=True)
+                qd = q_h.to(dev, non_blocking=True)
+                if is_hamming:
+                    i, d_ = mvd.sharded_hamming_knn(sd, qd, k, id_offset=lo)
+                else:
+                    i, d_ = mvd.sharded_brute_force_knn(sd, qd, k, metric, id_offset=lo)
+                return i.cpu(), d_.cpu()
+        e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        te = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - te
+        barrier()
+        if world > 1:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        h2d = shard.numel() * shard.element_size() + q.numel() * q.element_size()
+        d2h = w["nq"] * k * 8
+        e2e = {"value": w["nq"] * args.e2e_steps / e2e_s, "unit": "queries/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "steps": args.e2e_steps, "path": "mlxvs_brute_force_knn (C API, host buffers)"
+               if world == 1 else "mlxvs_b200.distributed on pinned host buffers"}
+
+    # roofline of the dominant kernel (rank 0's launches)
+    roof = None
+    if kern_launches > 0:
+        per_launch_s = kern_ms / kern_launches / 1e3
+        n_local = hi - lo
+        if is_hamming:
+            # integer work: 32-bit popcounts per launch; reported against the
+            # HBM copy bandwidth is meaningless here (compute bound), so the
+            # unit is the popcount rate
+            words = w["bytes"] // 4
+            pops = w["nq"] * n_local * words
+            roof = {"bound": "int-pipe", "achieved": pops / per_launch_s / 1e12,
+                    "unit": "Tpopc32/s", "peak": None, "frac": None, "traffic": None,
+                    "kernel": kname, "kernel_ms": per_launch_s * 1e3,
+                    "algorithmic_per_launch": f"{pops:.3e} 32-bit popcounts"}
+        else:
+            flops = 2.0 * w["nq"] * n_local * w["d"]
+            ach = flops / per_launch_s / 1e12
+            peak = peaks["bf16_sustained"]
+            roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                    "frac": ach / peak, "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
+                    "peak_source": f"{peaks['source']} bf16 sustained (the kernel runs back to "
+                                   f"back for the whole timed region)",
+                    "frac_of_burst": ach / peaks["bf16"], "kernel": kname,
+                    "kernel_ms": per_launch_s * 1e3,
+                    "algorithmic_per_launch": f"2*Q*N*D = {flops:.3e} FLOP"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base_np = shard.cpu().numpy()
+        q_np = q.cpu().numpy()
+        rate, m, t = cpu_sample_rate(w, base_np, q_np, args.cpu_budget)
+        cpu = {"value": rate, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{m} queries against all {w['n']} base rows ({t:.1f} s, OpenMP on "
+                         f"every host core)"}
+
+    if rank == 0:
+        value = w["nq"] * args.steps / (elapsed_ms / 1e3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "u8" if is_hamming else "f16",
+            "data": "synthetic (seeded, BASELINE distributions)",
+            "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
+                       "queries": w["nq"], "k": k,
+                       "parallelism": f"base rows sharded over {world} GPU(s)",
+                       "l2_flush": "inputs larger than L2 (fp32 base 512 MB)"
+                       if not is_hamming else "inputs larger than L2"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(all_launches), "clocks": clocks,
+            "check_vs_oracle_4_queries": check,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -197,6 +197,20 @@ MLXVS_C_API int mlxvs_merge_keys_device(
  */
 MLXVS_C_API int mlxvs_device_synchronize(void* stream);
 
+/**
+ * Benchmark support (not in the reference): when on, every launch of this
+ * library's kernels is bracketed by CUDA events on its stream.  Turning it
+ * on or off clears the records.
+ */
+MLXVS_C_API int mlxvs_profile_enable(int32_t on);
+
+/**
+ * Total device time in ms and launch count of the recorded launches of one
+ * kernel ("prep", "gemm_topk", "merge", "hamming_topk", "sumsq", "fill"), or
+ * of all of them when kernel is NULL.  Waits for the recorded events.
+ */
+MLXVS_C_API int mlxvs_profile_read(const char* kernel, double* total_ms, int64_t* launches);
+
 #ifdef __cplusplus
 }
 #endif

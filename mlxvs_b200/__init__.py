@@ -74,6 +74,9 @@ def _load():
         "mlxvs_hamming_keys_device": [p, i64, p, i64, i32, i32, i64, p, p],
         "mlxvs_merge_keys_device": [p, i32, i64, i32, i32, p, i32, p, p, p],
         "mlxvs_device_synchronize": [p],
+        "mlxvs_profile_enable": [i32],
+        "mlxvs_profile_read": [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
+                               ctypes.POINTER(ctypes.c_int64)],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -313,3 +316,17 @@ def synchronize(stream=None, device=None):
     dev = device if device is not None else torch.cuda.current_device()
     with torch.cuda.device(dev):
         _check(_load().mlxvs_device_synchronize(_stream_handle(stream, dev)))
+
+
+def profile_enable(on=True):
+    """Brackets every kernel launch with CUDA events (benchmarks); clears records."""
+    _check(_load().mlxvs_profile_enable(1 if on else 0))
+
+
+def profile_read(kernel=None):
+    """(total device ms, launches) of the recorded launches of one kernel, or all."""
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_int64(0)
+    name = kernel.encode() if kernel else None
+    _check(_load().mlxvs_profile_read(name, ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value

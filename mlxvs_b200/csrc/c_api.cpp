@@ -217,6 +217,14 @@ int mlxvs_merge_keys_device(const uint64_t* lists, int32_t num_lists, int64_t nq
   });
 }
 
+int mlxvs_profile_enable(int32_t on) {
+  return guarded([&] { mlxvs_b200::profile_enable(on != 0); });
+}
+
+int mlxvs_profile_read(const char* kernel, double* total_ms, int64_t* launches) {
+  return guarded([&] { mlxvs_b200::profile_read(kernel, total_ms, launches); });
+}
+
 int mlxvs_device_synchronize(void* stream) {
   return guarded([&] { mlxvs_b200::device_synchronize(static_cast<cudaStream_t>(stream)); });
 }

@@ -77,6 +77,41 @@ DeviceInfo& device_info() {
   return info;
 }
 
+// ------------------------------------------------------------- profiling
+// When enabled, every launch of the library's kernels is bracketed by CUDA
+// events recorded on the launching stream; profile_read sums their device
+// times per kernel name.  Off by default (benchmarks turn it on).
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+std::mutex prof_mu;
+bool prof_on = false;
+std::vector<ProfRecord> prof_records;
+
+struct ProfScope {
+  const char* name;
+  cudaStream_t s;
+  cudaEvent_t start = nullptr, stop = nullptr;
+  ProfScope(const char* n, cudaStream_t st) : name(n), s(st) {
+    bool on;
+    {
+      std::lock_guard<std::mutex> g(prof_mu);
+      on = prof_on;
+    }
+    if (!on) return;
+    CK(cudaEventCreate(&start));
+    CK(cudaEventCreate(&stop));
+    CK(cudaEventRecord(start, s));
+  }
+  ~ProfScope() {
+    if (!start) return;
+    cudaEventRecord(stop, s);
+    std::lock_guard<std::mutex> g(prof_mu);
+    prof_records.push_back({name, start, stop});
+  }
+};
+
 // Scratch buffers of one call, returned to the pool in stream order.
 struct Scratch {
   cudaStream_t s;
@@ -160,6 +195,7 @@ void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
   int64_t blocks = std::min<int64_t>((p.n_pad + 7) / 8, (int64_t)sms * 16);
   bool vec = p.lo == nullptr && !p.cosine && p.d % 4 == 0 &&
              (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+  ProfScope prof("prep", s);
   if (vec)
     prep_rows_vec4_kernel<<<(unsigned)blocks, threads, 0, s>>>(p);
   else
@@ -175,6 +211,7 @@ void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64
   int cap = 2;
   while (cap < total && cap < MERGE_CAP) cap <<= 1;
   while (cap <= k) cap <<= 1;
+  ProfScope prof("merge", s);
   merge_keys_kernel<<<(unsigned)nq, MERGE_THREADS, (size_t)cap * 8, s>>>(
       lists, num_lists, list_rows, nq, k, kind, qq, out_keys, ids, dist, cap);
   CK(cudaGetLastError());
@@ -184,17 +221,19 @@ void launch_fill(int64_t count, int kind, int32_t* ids, float* dist, uint64_t* k
                  cudaStream_t s) {
   if (count == 0) return;
   unsigned blocks = (unsigned)std::min<int64_t>((count + 255) / 256, 4096);
+  ProfScope prof("fill", s);
   fill_missing_kernel<<<blocks, 256, 0, s>>>(count, kind, ids, dist, keys);
   CK(cudaGetLastError());
 }
 
-template <int QB, int NPASS>
+template <int QB, int NPASS, int CG>
 void launch_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                  const CUtensorMap& b_lo, const KnnGemmParams& p, int grid, uint32_t smem,
                  cudaStream_t s) {
-  auto kern = knn_gemm_topk_kernel<QB, NPASS>;
+  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<grid, GemmLayout<QB, NPASS>::THREADS, smem, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+  ProfScope prof("gemm_topk", s);
+  kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(a_hi, a_lo, b_hi, b_lo, p);
   CK(cudaGetLastError());
 }
 
@@ -281,30 +320,33 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
     out_scale = std::ldexp(1.0f, -(eb + eq));
   }
 
-  // kernel shape: 128 queries per CTA when the heaps fit (64, 32 or 16 for
-  // large k: the MMA still computes 128 rows, the rest of the lanes are unused),
-  // the query block resident in shared memory when it fits with >= 3 stages
+  // kernel shape, in order of preference: 128 queries per CTA with the
+  // 256 columns of a tile split over two warp groups (two heaps per query),
+  // then one warp group, then 64 .. 8 queries per CTA for large k (the MMA
+  // still computes 128 rows; the other lanes are unused); the query block
+  // resident in shared memory when it fits; the deepest ring that fits
   const int npa = exact ? 1 : 2;
   const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
-  int QB = 0, stages = 0, a_stream = 0;
-  for (int pass = 0; pass < 3 && QB == 0; ++pass) {
-    const int min_stages = pass < 2 ? 3 : 2;
-    for (int qb : {128, 64, 32, 16}) {
-      if (pass == 0 && qb != 128) continue;  // first try 128 only
-      for (int as : {0, 1}) {
-        for (int st = 8; st >= min_stages; --st) {
-          GemmSmem lay = gemm_smem(qb, npa, kchunks, st, as, k);
-          if (lay.total <= budget) {
-            QB = qb;
-            stages = st;
-            a_stream = as;
-            break;
-          }
+  int QB = 0, CG = 0, stages = 0, a_stream = 0;
+  const int want_stages = exact ? 3 : 2;
+  struct Shape { int qb, cg, min_st; };
+  const Shape order[] = {{128, 2, want_stages}, {128, 1, want_stages}, {64, 1, want_stages},
+                         {32, 1, want_stages},  {16, 1, want_stages},  {8, 1, want_stages},
+                         {128, 2, 2}, {128, 1, 2}, {64, 1, 2}, {32, 1, 2}, {16, 1, 2}, {8, 1, 2}};
+  for (const Shape& sh : order) {
+    for (int as : {0, 1}) {
+      for (int st = 8; st >= sh.min_st; --st) {
+        if (gemm_smem(sh.qb, npa, sh.cg, kchunks, st, as, k).total <= budget) {
+          QB = sh.qb;
+          CG = sh.cg;
+          stages = st;
+          a_stream = as;
+          break;
         }
-        if (QB) break;
       }
       if (QB) break;
     }
+    if (QB) break;
   }
   if (QB == 0) throw std::runtime_error("[mlxvs_b200] no kernel shape fits shared memory");
   const int qblocks = (int)((nq + QB - 1) / QB);
@@ -340,30 +382,23 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.out_scale = out_scale;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
-  const GemmSmem lay = gemm_smem(QB, npa, kchunks, stages, a_stream, k);
+  const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k);
   const uint32_t smem = lay.total + 1024u;
   const int grid = std::min(units, dev.sms);
-  if (QB == 128) {
-    if (exact)
-      launch_gemm<128, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-    else
-      launch_gemm<128, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-  } else if (QB == 64) {
-    if (exact)
-      launch_gemm<64, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-    else
-      launch_gemm<64, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-  } else if (QB == 32) {
-    if (exact)
-      launch_gemm<32, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-    else
-      launch_gemm<32, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-  } else {
-    if (exact)
-      launch_gemm<16, 1>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
-    else
-      launch_gemm<16, 3>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s);
+#define MLXVS_GEMM(QB_, CG_)                                                   \
+  if (QB == QB_ && CG == CG_) {                                              \
+    if (exact)                                                               \
+      launch_gemm<QB_, 1, CG_>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s); \
+    else                                                                     \
+      launch_gemm<QB_, 3, CG_>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s); \
   }
+  MLXVS_GEMM(128, 2)
+  MLXVS_GEMM(128, 1)
+  MLXVS_GEMM(64, 1)
+  MLXVS_GEMM(32, 1)
+  MLXVS_GEMM(16, 1)
+  MLXVS_GEMM(8, 1)
+#undef MLXVS_GEMM
   launch_merge(partial, splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s);
 }
 
@@ -396,8 +431,11 @@ void launch_hamming_t(HammingParams p, const DeviceInfo& dev, Scratch& sc, const
   p.units = p.qblocks * p.splits;
   p.partial = sc.alloc<uint64_t>((size_t)p.splits * p.nq_pad * p.k);
   const int grid = std::min(p.units, slots);
-  kern<<<grid, QH + 32, smem, s>>>(p);
-  CK(cudaGetLastError());
+  {
+    ProfScope prof("hamming_topk", s);
+    kern<<<grid, QH + 32, smem, s>>>(p);
+    CK(cudaGetLastError());
+  }
   launch_merge(p.partial, p.splits, p.nq_pad, p.nq, p.k, KIND_HAMMING, nullptr, out.keys, out.ids,
                out.dist, s);
 }
@@ -526,6 +564,7 @@ void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kin
             "[mlxvs::merge_keys] L2 distances need the queries [nq, d].");
     qq = sc.alloc<float>((size_t)nq);
     unsigned blocks = (unsigned)std::min<int64_t>((nq + 7) / 8, (int64_t)dev.sms * 16);
+    ProfScope prof("sumsq", s);
     row_sumsq_kernel<<<blocks, 256, 0, s>>>(queries, nq, d, qq);
     CK(cudaGetLastError());
   }
@@ -546,6 +585,32 @@ void device_synchronize(cudaStream_t s) {
     throw std::runtime_error("[mlxvs_b200] a kernel gave up waiting (error word " +
                              std::to_string(err) + ")");
   }
+}
+
+void profile_enable(bool on) {
+  std::lock_guard<std::mutex> g(prof_mu);
+  for (auto& r : prof_records) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  prof_records.clear();
+  prof_on = on;
+}
+
+void profile_read(const char* name, double* total_ms, int64_t* launches) {
+  std::lock_guard<std::mutex> g(prof_mu);
+  double ms = 0.0;
+  int64_t count = 0;
+  for (auto& r : prof_records) {
+    if (name && std::strcmp(name, r.name) != 0) continue;
+    CK(cudaEventSynchronize(r.stop));
+    float t = 0.0f;
+    CK(cudaEventElapsedTime(&t, r.start, r.stop));
+    ms += t;
+    ++count;
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = count;
 }
 
 const char* version() { return MLXVS_B200_VERSION; }

@@ -48,6 +48,16 @@ void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kin
  * on the current device (and clears it). */
 void device_synchronize(cudaStream_t s);
 
+/** Per-kernel device times for benchmarks: when on, launches are bracketed
+ * by CUDA events on their stream.  Enabling (or disabling) clears the
+ * records. */
+void profile_enable(bool on);
+
+/** Sum of the recorded device times (ms) and launch count of the kernels
+ * named `name` ("prep", "gemm_topk", "merge", "hamming_topk", "sumsq",
+ * "fill"), or of all of them when name is null.  Waits for the events. */
+void profile_read(const char* name, double* total_ms, int64_t* launches);
+
 /** Version string. */
 const char* version();
 

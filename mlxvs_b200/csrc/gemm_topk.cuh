@@ -36,7 +36,7 @@ constexpr int GT_BN = 256;       // base rows per tile (MMA N)
 constexpr int GT_KCH = 64;       // fp16 columns per K chunk (one 128-byte swizzle row)
 constexpr int GT_ACHUNK = 128 * 128;  // bytes of one A chunk (128 rows x 128 B)
 constexpr int GT_BCHUNK = GT_BN * 128;  // bytes of one B chunk
-constexpr int GT_SHARE_TILES = 4;  // tiles between exchanges of the shared floor
+constexpr int GT_SHARE_TILES = 2;  // tiles between exchanges of the shared floor (power of 2)
 
 struct KnnGemmParams {
   int32_t qblocks;   // query blocks of QB rows
@@ -59,9 +59,16 @@ struct KnnGemmParams {
   uint64_t wait_ns;                // limit of every wait
 };
 
-template <int QB, int NPASS>
+template <int QB, int NPASS, int CG>
 struct GemmLayout {
-  static constexpr int EW = QB >= 32 ? QB / 32 : 1;  // epilogue warps
+  // CG column groups of 4 epilogue warps: warp w reads TMEM lane quarter
+  // w % 4 (the hardware's rule) and column group w / 4 of each 256-column
+  // accumulator; each (column group, query) keeps its own heap
+  static constexpr int EW = 4 * CG;
+  static constexpr int ROW_GROUPS = QB >= 32 ? QB / 32 : 1;
+  static constexpr int ACTIVE_EW = CG * ROW_GROUPS;  // warps holding queries
+  static constexpr int PRODUCER = EW;
+  static constexpr int MMA = EW + 1;
   static constexpr int THREADS = (EW + 2) * 32;
   static constexpr int NPA = NPASS == 1 ? 1 : 2;  // operand planes: hi (, lo)
 };
@@ -70,12 +77,13 @@ struct GemmLayout {
 struct GemmSmem {
   uint32_t a_off, a_bytes;      // resident query block (0 bytes when streamed)
   uint32_t stage_off, stage_bytes;
-  uint32_t heap_off, heap_bytes;
+  uint32_t heap_off, heap_bytes;  // [k][CG * QB] keys: a heap per (column group, query)
+  uint32_t nb_off;                // [4 * CG warps][256 / CG] floats: the tile's per-row terms
   uint32_t bar_off;
   uint32_t total;
 };
 
-__host__ __device__ inline GemmSmem gemm_smem(int QB, int npa, int kchunks, int stages,
+__host__ __device__ inline GemmSmem gemm_smem(int QB, int npa, int cg, int kchunks, int stages,
                                               int a_stream, int k) {
   GemmSmem s;
   s.a_off = 0;
@@ -83,8 +91,9 @@ __host__ __device__ inline GemmSmem gemm_smem(int QB, int npa, int kchunks, int 
   s.stage_off = s.a_off + s.a_bytes;
   s.stage_bytes = (uint32_t)(npa * (GT_BCHUNK + (a_stream ? GT_ACHUNK : 0)));
   s.heap_off = s.stage_off + (uint32_t)stages * s.stage_bytes;
-  s.heap_bytes = (uint32_t)(QB * k * 8);
-  s.bar_off = (s.heap_off + s.heap_bytes + 15u) & ~15u;
+  s.heap_bytes = (uint32_t)(cg * QB * k * 8);
+  s.nb_off = (s.heap_off + s.heap_bytes + 15u) & ~15u;
+  s.bar_off = s.nb_off + 4u * GT_BN * 4u;
   // full[stages], empty[stages], a_full, a_empty, acc_full[2], acc_empty[2], aux
   s.total = s.bar_off + (uint32_t)(2 * stages + 7) * 8u + 16u;
   return s;
@@ -92,28 +101,28 @@ __host__ __device__ inline GemmSmem gemm_smem(int QB, int npa, int kchunks, int 
 
 #ifdef __CUDACC__
 
-// Replaces the root of a min-heap of k keys (slot s of this thread's heap at
-// heap[s * QB]) by key, which is larger than the root.
-template <int QB>
+// Replaces the root of a min-heap of k keys (slot s at heap[s * HS]) by key,
+// which is larger than the root.
+template <int HS>
 __device__ __forceinline__ void heap_replace_root(uint64_t* heap, int k, uint64_t key) {
   int i = 0;
   for (;;) {
     int l = 2 * i + 1;
     if (l >= k) break;
-    uint64_t mv = heap[l * QB];
+    uint64_t mv = heap[l * HS];
     int m = l;
     if (l + 1 < k) {
-      uint64_t rv = heap[(l + 1) * QB];
+      uint64_t rv = heap[(l + 1) * HS];
       if (rv < mv) {
         mv = rv;
         m = l + 1;
       }
     }
     if (mv >= key) break;
-    heap[i * QB] = mv;
+    heap[i * HS] = mv;
     i = m;
   }
-  heap[i * QB] = key;
+  heap[i * HS] = key;
 }
 
 struct EpiState {
@@ -122,24 +131,15 @@ struct EpiState {
   float thr;       // score of floor (-inf when none): the fast rejection test
 };
 
-// The slow path of a chunk whose best score reached the floor: every score of
-// the chunk is tried against the heap.  Out of line (it is rare), the state
-// passed and returned by value so that it stays in registers.
-template <int QB>
-__device__ __noinline__ EpiState epi_insert_chunk(const float (&v)[32], int64_t col0,
-                                                  int64_t n_valid, int64_t id_offset,
-                                                  uint64_t* heap, int k, EpiState st) {
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (v[j] >= st.thr && col0 + j < n_valid) {
-      uint64_t key = make_key(v[j], (uint32_t)(id_offset + col0 + j));
-      if (key > st.floor) {
-        heap_replace_root<QB>(heap, k, key);
-        uint64_t root = heap[0];
-        st.floor = root > st.gfl ? root : st.gfl;
-        st.thr = key_score(st.floor);
-      }
-    }
+// One candidate against the heap, out of line (the slow path is rare); the
+// state travels by value so it stays in registers.
+template <int HS>
+__device__ __noinline__ EpiState heap_offer(uint64_t* heap, int k, uint64_t key, EpiState st) {
+  if (key > st.floor) {
+    heap_replace_root<HS>(heap, k, key);
+    uint64_t root = heap[0];
+    st.floor = root > st.gfl ? root : st.gfl;
+    st.thr = key_score(st.floor);
   }
   return st;
 }
@@ -158,51 +158,75 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
-template <int QB>
-__device__ __forceinline__ void epi_chunk(const uint32_t (&r)[32], const float* nbp, int64_t col0,
-                                          const KnnGemmParams& p, uint64_t* heap,
-                                          EpiState& st) {
-  float v[32];
-  const float4* nb4 = reinterpret_cast<const float4*>(nbp);
-#pragma unroll
-  for (int j4 = 0; j4 < 8; ++j4) {
-    float4 t = __ldg(nb4 + j4);
-    v[4 * j4 + 0] = __uint_as_float(r[4 * j4 + 0]) - t.x;
-    v[4 * j4 + 1] = __uint_as_float(r[4 * j4 + 1]) - t.y;
-    v[4 * j4 + 2] = __uint_as_float(r[4 * j4 + 2]) - t.z;
-    v[4 * j4 + 3] = __uint_as_float(r[4 * j4 + 3]) - t.w;
-  }
-  float m[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) m[j] = fmaxf(v[j], v[j + 16]);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], m[j + 8]);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) m[j] = fmaxf(m[j], m[j + 4]);
-  float mx = fmaxf(fmaxf(m[0], m[2]), fmaxf(m[1], m[3]));
-  if (mx >= st.thr && (QB >= 32 || (threadIdx.x & 31) < QB))
-    st = epi_insert_chunk<QB>(v, col0, p.n_valid, p.id_offset, heap, p.k, st);
+__device__ __forceinline__ void sub2(float& a, float& b, float c, float d) {
+  uint64_t x, y, z;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(c), "f"(d));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(z));
 }
 
-template <int QB, int NPASS>
-__global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
+// with one compare when their max is below the floor, else offer each.
+template <int HS>
+__device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const float* nbs,
+                                          int64_t col0, const KnnGemmParams& p, bool row_on,
+                                          uint64_t* heap, EpiState& st) {
+  float v[16];
+  const float4* nb4 = reinterpret_cast<const float4*>(nbs);
+#pragma unroll
+  for (int j4 = 0; j4 < 4; ++j4) {
+    float4 t = nb4[j4];
+    v[4 * j4 + 0] = __uint_as_float(r[o + 4 * j4 + 0]);
+    v[4 * j4 + 1] = __uint_as_float(r[o + 4 * j4 + 1]);
+    v[4 * j4 + 2] = __uint_as_float(r[o + 4 * j4 + 2]);
+    v[4 * j4 + 3] = __uint_as_float(r[o + 4 * j4 + 3]);
+    sub2(v[4 * j4 + 0], v[4 * j4 + 1], t.x, t.y);
+    sub2(v[4 * j4 + 2], v[4 * j4 + 3], t.z, t.w);
+  }
+  float m0 = max3(v[0], v[1], v[2]);
+  float m1 = max3(v[3], v[4], v[5]);
+  float m2 = max3(v[6], v[7], v[8]);
+  float m3 = max3(v[9], v[10], v[11]);
+  float m4 = max3(v[12], v[13], v[14]);
+  float mx = max3(max3(m0, m1, m2), max3(m3, m4, v[15]), -INFINITY);
+  if (mx >= st.thr && row_on) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (v[j] >= st.thr && col0 + j < p.n_valid)
+        st = heap_offer<HS>(heap, p.k, make_key(v[j], (uint32_t)(p.id_offset + col0 + j)), st);
+    }
+  }
+}
+
+template <int QB, int NPASS, int CG>
+__global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     knn_gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                          const __grid_constant__ CUtensorMap tm_a_lo,
                          const __grid_constant__ CUtensorMap tm_b_hi,
                          const __grid_constant__ CUtensorMap tm_b_lo, const KnnGemmParams p) {
-  using L = GemmLayout<QB, NPASS>;
-  constexpr int EW = L::EW;
+  using L = GemmLayout<QB, NPASS, CG>;
   constexpr int NPA = L::NPA;
+  constexpr int HS = CG * QB;     // heap slot stride
+  constexpr int CW = GT_BN / CG;  // columns per epilogue warp per tile
+  constexpr int NCH = CW / 32;    // chunks of 32 columns (even)
   constexpr uint32_t IDESC = idesc_f16_f32(128, GT_BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const GemmSmem lay = gemm_smem(QB, NPA, p.kchunks, p.stages, p.a_stream, p.k);
+  const GemmSmem lay = gemm_smem(QB, NPA, CG, p.kchunks, p.stages, p.a_stream, p.k);
   uint8_t* a_res = smem + lay.a_off;
   uint8_t* stage_base = smem + lay.stage_off;
   uint64_t* heap_all = reinterpret_cast<uint64_t*>(smem + lay.heap_off);
+  float* nb_all = reinterpret_cast<float*>(smem + lay.nb_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + lay.bar_off);
   uint64_t* full = bars;
   uint64_t* empty = bars + p.stages;
@@ -225,12 +249,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
     mbar_init(a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EW);
+      mbar_init(&acc_empty[b], L::ACTIVE_EW);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == EW + 1) {
+  if (warp == L::MMA) {
     tmem_alloc(tmem_slot, 2 * GT_BN);
     tmem_relinquish();
   }
@@ -239,7 +263,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == EW) {
+  if (warp == L::PRODUCER) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0) {
       tma_prefetch_desc(&tm_a_hi);
@@ -279,11 +303,13 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
             mbar_arrive_expect_tx(&full[stage],
                                   (uint32_t)(NPA * GT_BCHUNK) + (p.a_stream ? a_bytes : 0u));
             tma_load_2d(st, &tm_b_hi, &full[stage], kc * GT_KCH, t * GT_BN);
-            if (NPASS == 3) tma_load_2d(st + GT_BCHUNK, &tm_b_lo, &full[stage], kc * GT_KCH, t * GT_BN);
+            if (NPASS == 3)
+              tma_load_2d(st + GT_BCHUNK, &tm_b_lo, &full[stage], kc * GT_KCH, t * GT_BN);
             if (p.a_stream) {
               uint8_t* sa = st + NPA * GT_BCHUNK;
               tma_load_2d(sa, &tm_a_hi, &full[stage], kc * GT_KCH, qb * QB);
-              if (NPASS == 3) tma_load_2d(sa + GT_ACHUNK, &tm_a_lo, &full[stage], kc * GT_KCH, qb * QB);
+              if (NPASS == 3)
+                tma_load_2d(sa + GT_ACHUNK, &tm_a_lo, &full[stage], kc * GT_KCH, qb * QB);
             }
             if (++stage == (uint32_t)p.stages) {
               stage = 0;
@@ -299,12 +325,11 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
       // Every load issued lands before the CTA may exit: the last arm of each
       // stage completes by itself (bounded wait all the same).
       for (int s = 0; s < p.stages; ++s) {
-        // the stage's most recent arm had parity (phase of that arm)
         uint32_t par = ((uint32_t)s < stage) ? phase : (phase ^ 1);
         mbar_wait(&full[s], par, abort_flag, p.wait_ns);
       }
     }
-  } else if (warp == EW + 1) {
+  } else if (warp == L::MMA) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_ph = 0, uidx = 0;
@@ -377,12 +402,15 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
       umma_commit(a_empty);
       mbar_wait(a_empty, (p.a_stream ? 0u : uidx) & 1, abort_flag, p.wait_ns);
     }
-  } else {
+  } else if (warp < L::EW && (warp & 3) < L::ROW_GROUPS) {
     // ------------------------------------------------------------- epilogue
-    const int row = warp * 32 + lane;  // TMEM lane = query within the block
+    const int rg = warp & 3;          // TMEM lane quarter
+    const int ch = warp >> 2;         // column group of the tile
+    const int row = rg * 32 + lane;   // query within the block
     // with QB < 32 the lanes past QB only join the warp-collective loads
     const bool row_on = row < QB;
-    uint64_t* heap = heap_all + (row_on ? row : 0);
+    uint64_t* heap = heap_all + ch * QB + (row_on ? row : 0);
+    float* nbw = nb_all + warp * CW;  // this warp's per-row terms of the tile
     uint32_t acc = 0, acc_ph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
@@ -393,42 +421,67 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
       const int64_t q = (int64_t)qb * QB + row;
       const bool q_ok = row_on && q < p.nq;
       if (row_on)
-        for (int s = 0; s < p.k; ++s) heap[s * QB] = 0;
+        for (int s = 0; s < p.k; ++s) heap[s * HS] = 0;
       EpiState st;
       st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q) : 0ull;
       st.floor = st.gfl;
       st.thr = key_score(st.floor);
+      float4 nbr[CW / 128];
+      if (t0 < t1) {
+#pragma unroll
+        for (int i = 0; i < CW / 128; ++i)
+          nbr[i] = __ldg(reinterpret_cast<const float4*>(p.nb + (int64_t)t0 * GT_BN + ch * CW) +
+                         lane + 32 * i);
+      }
       for (int t = t0; t < t1; ++t) {
+        // stage this tile's per-row terms, prefetch the next tile's
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < CW / 128; ++i) reinterpret_cast<float4*>(nbw)[lane + 32 * i] = nbr[i];
+        __syncwarp();
+        if (t + 1 < t1) {
+#pragma unroll
+          for (int i = 0; i < CW / 128; ++i)
+            nbr[i] = __ldg(
+                reinterpret_cast<const float4*>(p.nb + (int64_t)(t + 1) * GT_BN + ch * CW) +
+                lane + 32 * i);
+        }
         if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + acc * GT_BN;
-        const int64_t col_base = (int64_t)t * GT_BN;
-        const float* nbp = p.nb + col_base;
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(rg * 32) << 16) + acc * GT_BN + (uint32_t)(ch * CW);
+        const int64_t col_base = (int64_t)t * GT_BN + ch * CW;
         uint32_t ra[32], rb[32];
         tmem_ld32(taddr, ra);
         tmem_wait_ld_regs(ra);
 #pragma unroll 1
-        for (int c = 0; c < GT_BN / 32; c += 2) {
-          // tcgen05.ld is warp-collective: reconverge after a divergent slow path
+        for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          epi_chunk<QB>(ra, nbp + c * 32, col_base + c * 32, p, heap, st);
+          epi_sub16<HS>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, st);
+          epi_sub16<HS>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, st);
           __syncwarp();
           tmem_wait_ld_regs(rb);
-          if (c + 2 < GT_BN / 32) tmem_ld32(taddr + (c + 2) * 32, ra);
-          epi_chunk<QB>(rb, nbp + (c + 1) * 32, col_base + (c + 1) * 32, p, heap, st);
-          __syncwarp();
-          if (c + 2 < GT_BN / 32) tmem_wait_ld_regs(ra);
+          if (c + 2 < NCH) {
+            tmem_ld32(taddr + (c + 2) * 32, ra);
+          } else {
+            // the accumulator is free once its last columns are in registers
+            tc_fence_before();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          epi_sub16<HS>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, st);
+          epi_sub16<HS>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, st);
+          if (c + 2 < NCH) {
+            __syncwarp();
+            tmem_wait_ld_regs(ra);
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;
-        if (q_ok && ((t - t0) % GT_SHARE_TILES) == GT_SHARE_TILES - 1) {
+        if (q_ok && ((t - t0) & (GT_SHARE_TILES - 1)) == GT_SHARE_TILES - 1) {
           const uint64_t root = heap[0];
           uint64_t g;
           if (root != 0) {
@@ -447,15 +500,28 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
         }
       }
       if (!ok) break;
-      if (row_on && q < p.nq_pad) {
+      if (CG == 2) {
+        // the two column groups of each query meet: group 1's heap goes into
+        // group 0's, which is written out as the unit's list for the query
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+        if (ch == 0 && row_on) {
+          const uint64_t* other = heap + QB;
+          for (int s = 0; s < p.k; ++s) {
+            const uint64_t key = other[s * HS];
+            if (key > heap[0]) heap_replace_root<HS>(heap, p.k, key);
+          }
+        }
+      }
+      if (ch == 0 && row_on) {
         uint64_t* out = p.partial + ((size_t)split * p.nq_pad + q) * p.k;
         for (int s = 0; s < p.k; ++s) {
-          uint64_t key = heap[s * QB];
+          uint64_t key = heap[s * HS];
           if (key != 0 && p.out_scale != 1.0f)
             key = make_key(key_score(key) * p.out_scale, ~(uint32_t)key);
           out[s] = key;
         }
       }
+      if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
     }
     if (!ok) {
       *abort_flag = 1;
@@ -466,7 +532,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == EW + 1) tmem_dealloc(tmem_base, 2 * GT_BN);
+  if (warp == L::MMA) tmem_dealloc(tmem_base, 2 * GT_BN);
 }
 
 #endif  // __CUDACC__

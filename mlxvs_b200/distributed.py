@@ -1,0 +1,67 @@
+"""Row-sharded exact k-NN across the GPUs of one node.
+
+One process per GPU (torch.distributed, NCCL).  The base rows are split into
+contiguous shards; every rank searches its shard for all queries with the
+fused kernel, ids offset by the shard's first row (mlxvs_knn_keys_device),
+so that each rank holds its k best candidates per query as 64-bit keys.
+One all-gather of the [nq, k] keys (8 * nq * k bytes per rank) over NVLink
+is the only exchange; the merge kernel then keeps the k best of the
+world * k candidates per query (ties to the lower id, the reference's order)
+and converts them to distances.  Lower ranks hold lower ids, so the result
+equals the single-GPU search bit for bit.
+
+This replaces the reference's single-device tile loop (src/knn.cpp:104-121,
+merges at :117) with a cross-device one; the reference has no multi-GPU
+path.
+"""
+
+import torch
+import torch.distributed as dist
+
+from . import KIND_HAMMING, Metric, _metric, hamming_keys, knn_keys, merge_keys
+
+__all__ = ["shard_bounds", "gather_lists", "sharded_brute_force_knn", "sharded_hamming_knn"]
+
+
+def shard_bounds(n, world):
+    """Row ranges [b[r], b[r+1]) of the world's shards: contiguous, in rank order."""
+    return [(r * n) // world for r in range(world + 1)]
+
+
+def gather_lists(keys, group=None):
+    """All ranks' [nq, k] key lists as one [world, nq, k] tensor (rank order)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return keys.unsqueeze(0)
+    keys = keys.contiguous()
+    if keys.is_cuda:
+        out = torch.empty((world,) + tuple(keys.shape), dtype=keys.dtype, device=keys.device)
+        dist.all_gather_into_tensor(out, keys, group=group)
+        return out
+    parts = [torch.empty_like(keys) for _ in range(world)]
+    dist.all_gather(parts, keys, group=group)
+    return torch.stack(parts)
+
+
+def sharded_brute_force_knn(base_shard, queries, k, metric=Metric.l2, *, id_offset, group=None,
+                            stream=None):
+    """Exact k-NN of queries against the union of every rank's base shard.
+
+    base_shard and queries are CUDA tensors (queries identical on every
+    rank); id_offset is the global id of this shard's first row.  Returns
+    (ids int32 [nq, k], distances float32 [nq, k]) on every rank.
+    """
+    m = _metric(metric)
+    keys = knn_keys(base_shard, queries, k, m, id_offset=id_offset, stream=stream)
+    lists = gather_lists(keys, group)
+    return merge_keys(lists, k, m, queries if m == Metric.l2 else None, stream=stream)
+
+
+def sharded_hamming_knn(rows_shard, queries, k, *, id_offset, group=None, stream=None):
+    """Hamming version of sharded_brute_force_knn (uint8 codes)."""
+    keys = hamming_keys(rows_shard, queries, k, id_offset=id_offset, stream=stream)
+    lists = gather_lists(keys, group)
+    return merge_keys(lists, k, "hamming", stream=stream)
+
+
+KIND = {"hamming": KIND_HAMMING}
