@@ -235,6 +235,19 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
   return d;
 }
 
+// The same for a K-major tile of 16 fp16 per row in the 32-byte swizzled
+// layout (CU_TENSOR_MAP_SWIZZLE_32B): 32-byte rows, 8-row atoms of 256 bytes,
+// tile start 256-byte aligned; one K=16 step covers the whole row.
+__device__ __forceinline__ uint64_t sdesc_k32(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address, 16-byte units
+  d |= (uint64_t)1 << 16;                    // leading byte offset (unused here)
+  d |= (uint64_t)(256 >> 4) << 32;           // stride byte offset: 8 rows x 32 B
+  d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+  d |= (uint64_t)6 << 61;                    // swizzle mode: 32-byte
+  return d;
+}
+
 // Instruction descriptor of kind::f16: fp16 A and B, fp32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4)                       // D format: f32

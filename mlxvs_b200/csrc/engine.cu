@@ -152,9 +152,11 @@ EncodeTiledFn encode_fn() {
 }
 
 // 2-D fp16 tensor [rows, cols] (cols contiguous), tiles of box_cols x
-// box_rows written to shared memory with the 128-byte swizzle.
+// box_rows written to shared memory with the 128-byte swizzle (or the 32-byte
+// one for the 16-column |b|^2 pieces).
 CUtensorMap map_f16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
-                    uint32_t box_rows) {
+                    uint32_t box_rows,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   CUtensorMap m;
   std::memset(&m, 0, sizeof(m));
   cuuint64_t dims[2] = {cols, rows};
@@ -162,8 +164,8 @@ CUtensorMap map_f16(const void* base, uint64_t cols, uint64_t rows, uint32_t box
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("[mlxvs_b200] cuTensorMapEncodeTiled failed: " + std::to_string(r));
@@ -205,7 +207,7 @@ void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
 
 void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64_t nq, int k,
                   int kind, const float* qq, uint64_t* out_keys, int32_t* ids, float* dist,
-                  cudaStream_t s) {
+                  cudaStream_t s, float scale = 1.0f) {
   if (nq == 0) return;
   int64_t total = (int64_t)num_lists * k;
   int cap = 2;
@@ -213,7 +215,7 @@ void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64
   while (cap <= k) cap <<= 1;
   ProfScope prof("merge", s);
   merge_keys_kernel<<<(unsigned)nq, MERGE_THREADS, (size_t)cap * 8, s>>>(
-      lists, num_lists, list_rows, nq, k, kind, qq, out_keys, ids, dist, cap);
+      lists, num_lists, list_rows, nq, k, kind, qq, out_keys, ids, dist, cap, scale);
   CK(cudaGetLastError());
 }
 
@@ -226,14 +228,18 @@ void launch_fill(int64_t count, int kind, int32_t* ids, float* dist, uint64_t* k
   CK(cudaGetLastError());
 }
 
-template <int QB, int NPASS, int CG>
-void launch_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
-                 const CUtensorMap& b_lo, const KnnGemmParams& p, int grid, uint32_t smem,
+struct GemmMaps {
+  CUtensorMap a_hi, a_lo, b_hi, b_lo, b_x;
+};
+
+template <int QB, int NPASS, int CG, int NBM, int KR>
+void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t smem,
                  cudaStream_t s) {
-  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG>;
+  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   ProfScope prof("gemm_topk", s);
-  kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+  kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo,
+                                                              m.b_x, p);
   CK(cudaGetLastError());
 }
 
@@ -280,19 +286,27 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   __half* q_hi = sc.alloc<__half>((size_t)nq_pad * d_pad);
   float* nb = sc.alloc<float>((size_t)n_pad);
   float* qq = l2 ? sc.alloc<float>((size_t)nq_pad) : nullptr;
-  uint32_t* flags = sc.alloc<uint32_t>(4);
-  CK(cudaMemsetAsync(flags, 0, 16, s));
+  // |b|^2 as fp16 pieces for the extra K step (L2)
+  __half* b_x = l2 ? sc.alloc<__half>((size_t)n_pad * 16) : nullptr;
+  // flags: base inexact, base max |x|, query inexact, query max |x|, base
+  // |b|^2 not foldable
+  uint32_t* flags = sc.alloc<uint32_t>(8);
+  CK(cudaMemsetAsync(flags, 0, 32, s));
 
   PrepParams pb{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, 1.0f, b_hi, nullptr,
-                nb, l2 ? 1.0f : 0.0f, INFINITY, flags};
+                nb, l2 ? 1.0f : 0.0f, INFINITY, flags, b_x, flags + 4};
   PrepParams pq{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, 1.0f, q_hi,
-                nullptr, qq, 1.0f, 0.0f, flags + 2};
+                nullptr, qq, 1.0f, 0.0f, flags + 2, nullptr, nullptr};
   launch_prep(pb, dev.sms, s);
   launch_prep(pq, dev.sms, s);
-  uint32_t hflags[4];
-  CK(cudaMemcpyAsync(hflags, flags, 16, cudaMemcpyDeviceToHost, s));
+  uint32_t hflags[8];
+  CK(cudaMemcpyAsync(hflags, flags, 32, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
   const bool exact = hflags[0] == 0 && hflags[2] == 0;
+  // L2 on exact operands with integer |b|^2 < 2^31: -|b|^2 rides in the MMA
+  // and the epilogue reads scores straight from the accumulator
+  const bool fold = l2 && exact && hflags[4] == 0;
+  const int nbm = (!l2 || fold) ? 1 : 0;
 
   __half* b_lo = nullptr;
   __half* q_lo = nullptr;
@@ -312,9 +326,9 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
     b_lo = sc.alloc<__half>((size_t)n_pad * d_pad);
     q_lo = sc.alloc<__half>((size_t)nq_pad * d_pad);
     PrepParams pb2{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, b_lo,
-                   nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr};
+                   nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr, nullptr, nullptr};
     PrepParams pq2{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, sq, q_hi,
-                   q_lo, nullptr, 0.0f, 0.0f, nullptr};
+                   q_lo, nullptr, 0.0f, 0.0f, nullptr, nullptr, nullptr};
     launch_prep(pb2, dev.sms, s);
     launch_prep(pq2, dev.sms, s);
     out_scale = std::ldexp(1.0f, -(eb + eq));
@@ -327,18 +341,26 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   // resident in shared memory when it fits; the deepest ring that fits
   const int npa = exact ? 1 : 2;
   const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
-  int QB = 0, CG = 0, stages = 0, a_stream = 0;
-  const int want_stages = exact ? 3 : 2;
-  struct Shape { int qb, cg, min_st; };
-  const Shape order[] = {{128, 2, want_stages}, {128, 1, want_stages}, {64, 1, want_stages},
-                         {32, 1, want_stages},  {16, 1, want_stages},  {8, 1, want_stages},
-                         {128, 2, 2}, {128, 1, 2}, {64, 1, 2}, {32, 1, 2}, {16, 1, 2}, {8, 1, 2}};
+  int QB = 0, CG = 0, KR = 0, stages = 0, a_stream = 0;
+  const int want_stages = exact ? 4 : 2;
+  // k <= 16 keeps each query's list in registers (two column groups)
+  const int kr = k <= 8 ? 8 : (k <= 16 ? 16 : 0);
+  struct Shape { int qb, cg, kr, min_st; };
+  const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, 0, want_stages},
+                         {128, 1, 0, want_stages},  {64, 1, 0, want_stages},
+                         {32, 1, 0, want_stages},   {16, 1, 0, want_stages},
+                         {8, 1, 0, want_stages},    {128, 2, kr, 2},
+                         {128, 2, 0, 2},            {128, 1, 0, 2},
+                         {64, 1, 0, 2},             {32, 1, 0, 2},
+                         {16, 1, 0, 2},             {8, 1, 0, 2}};
   for (const Shape& sh : order) {
+    if (sh.cg == 2 && sh.kr == 0 && kr != 0) continue;  // the register list is the better form
     for (int as : {0, 1}) {
       for (int st = 8; st >= sh.min_st; --st) {
-        if (gemm_smem(sh.qb, npa, sh.cg, kchunks, st, as, k).total <= budget) {
+        if (gemm_smem(sh.qb, npa, sh.cg, kchunks, st, as, k, fold, sh.kr, nbm).total <= budget) {
           QB = sh.qb;
           CG = sh.cg;
+          KR = sh.kr;
           stages = st;
           a_stream = as;
           break;
@@ -357,11 +379,15 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   uint64_t* partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
   unsigned long long* gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
   CK(cudaMemsetAsync(gfloor, 0, (size_t)nq_pad * 8, s));
+  int* done = sc.alloc<int>((size_t)qblocks);
+  CK(cudaMemsetAsync(done, 0, (size_t)qblocks * 4, s));
 
-  CUtensorMap ta_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, QB);
-  CUtensorMap ta_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, QB);
-  CUtensorMap tb_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
-  CUtensorMap tb_lo = map_f16(b_lo ? b_lo : b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  GemmMaps maps;
+  maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, QB);
+  maps.a_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, QB);
+  maps.b_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  maps.b_lo = map_f16(b_lo ? b_lo : b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  maps.b_x = fold ? map_f16(b_x, 16, n_pad, 16, GT_BN, CU_TENSOR_MAP_SWIZZLE_32B) : maps.b_hi;
 
   KnnGemmParams p{};
   p.qblocks = qblocks;
@@ -372,6 +398,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.k = k;
   p.stages = stages;
   p.a_stream = a_stream;
+  p.extra = fold ? 1 : 0;
   p.n_valid = n;
   p.nq = nq;
   p.nq_pad = nq_pad;
@@ -379,27 +406,34 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.nb = nb;
   p.partial = partial;
   p.gfloor = gfloor;
+  p.done = done;
   p.out_scale = out_scale;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
-  const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k);
+  const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k, fold, KR, nbm);
   const uint32_t smem = lay.total + 1024u;
   const int grid = std::min(units, dev.sms);
-#define MLXVS_GEMM(QB_, CG_)                                                   \
-  if (QB == QB_ && CG == CG_) {                                              \
-    if (exact)                                                               \
-      launch_gemm<QB_, 1, CG_>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s); \
-    else                                                                     \
-      launch_gemm<QB_, 3, CG_>(ta_hi, ta_lo, tb_hi, tb_lo, p, grid, smem, s); \
+#define MLXVS_GEMM(QB_, CG_, KR_)                                           \
+  if (QB == QB_ && CG == CG_ && KR == KR_) {                                \
+    if (exact && nbm)                                                     \
+      launch_gemm<QB_, 1, CG_, 1, KR_>(maps, p, grid, smem, s);           \
+    else if (exact)                                                       \
+      launch_gemm<QB_, 1, CG_, 0, KR_>(maps, p, grid, smem, s);           \
+    else if (nbm)                                                         \
+      launch_gemm<QB_, 3, CG_, 1, KR_>(maps, p, grid, smem, s);           \
+    else                                                                  \
+      launch_gemm<QB_, 3, CG_, 0, KR_>(maps, p, grid, smem, s);           \
   }
-  MLXVS_GEMM(128, 2)
-  MLXVS_GEMM(128, 1)
-  MLXVS_GEMM(64, 1)
-  MLXVS_GEMM(32, 1)
-  MLXVS_GEMM(16, 1)
-  MLXVS_GEMM(8, 1)
+  MLXVS_GEMM(128, 2, 8)
+  MLXVS_GEMM(128, 2, 16)
+  MLXVS_GEMM(128, 2, 0)
+  MLXVS_GEMM(128, 1, 0)
+  MLXVS_GEMM(64, 1, 0)
+  MLXVS_GEMM(32, 1, 0)
+  MLXVS_GEMM(16, 1, 0)
+  MLXVS_GEMM(8, 1, 0)
 #undef MLXVS_GEMM
-  launch_merge(partial, splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s);
+  launch_merge(partial, splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s, out_scale);
 }
 
 // ------------------------------------------------------------------ Hamming

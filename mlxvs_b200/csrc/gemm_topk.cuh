@@ -36,7 +36,9 @@ constexpr int GT_BN = 256;       // base rows per tile (MMA N)
 constexpr int GT_KCH = 64;       // fp16 columns per K chunk (one 128-byte swizzle row)
 constexpr int GT_ACHUNK = 128 * 128;  // bytes of one A chunk (128 rows x 128 B)
 constexpr int GT_BCHUNK = GT_BN * 128;  // bytes of one B chunk
-constexpr int GT_SHARE_TILES = 2;  // tiles between exchanges of the shared floor (power of 2)
+constexpr int GT_XCHUNK = GT_BN * 32;   // bytes of a tile's |b|^2 pieces (16 fp16 per row)
+constexpr int GT_AX = 128 * 32;         // bytes of the constant query-side block
+constexpr int GT_SHARE_TILES = 1;  // tiles between exchanges of the shared floor (power of 2)
 
 struct KnnGemmParams {
   int32_t qblocks;   // query blocks of QB rows
@@ -47,6 +49,7 @@ struct KnnGemmParams {
   int32_t k;         // neighbors kept, <= heap capacity
   int32_t stages;    // depth of the base-chunk ring
   int32_t a_stream;  // 1: query chunks travel with the base chunks
+  int32_t extra;     // 1: one more K=16 block per tile accumulates -|b|^2 (L2)
   int64_t n_valid;   // base rows
   int64_t nq;        // queries
   int64_t nq_pad;    // query rows of the partial lists (multiple of QB)
@@ -54,11 +57,15 @@ struct KnnGemmParams {
   const float* nb;                 // [tiles * GT_BN]: subtracted from each dot
   uint64_t* partial;               // [splits][nq_pad][k] keys
   unsigned long long* gfloor;      // [nq_pad] shared floor keys (0 = none)
+  int* done;                       // [qblocks] 1 + the latest split whose lists are written
   float out_scale;                 // partial scores are written as score * out_scale
   uint32_t* err;                   // error word (bounded waits that gave up)
   uint64_t wait_ns;                // limit of every wait
 };
 
+// NBM = 0: the epilogue subtracts the per-row term nb from each dot (L2 when
+// |b|^2 cannot ride in the MMA); NBM = 1: the accumulator already is the
+// score (inner product, cosine, or L2 with the extra K block).
 template <int QB, int NPASS, int CG>
 struct GemmLayout {
   // CG column groups of 4 epilogue warps: warp w reads TMEM lane quarter
@@ -76,24 +83,34 @@ struct GemmLayout {
 // Shared-memory offsets, computed identically on host and device.
 struct GemmSmem {
   uint32_t a_off, a_bytes;      // resident query block (0 bytes when streamed)
+  uint32_t ax_off;              // the constant query-side block of the extra K step
   uint32_t stage_off, stage_bytes;
-  uint32_t heap_off, heap_bytes;  // [k][CG * QB] keys: a heap per (column group, query)
-  uint32_t nb_off;                // [4 * CG warps][256 / CG] floats: the tile's per-row terms
+  // heap mode: [k][CG * QB] keys, a heap per (column group, query); register
+  // mode: [k][QB] keys, column group 1's list handed to group 0 at unit end
+  uint32_t heap_off, heap_bytes;
+  uint32_t sv_off;                // register mode: [4 * CG warps][16][32] floats, slow-path scores
+  uint32_t nb_off;                // NBM 0: [4 * CG warps][256 / CG] floats, the tile's per-row terms
+  uint32_t fl_off;                // [CG][QB] keys: each group's current floor, for its partners
   uint32_t bar_off;
   uint32_t total;
 };
 
 __host__ __device__ inline GemmSmem gemm_smem(int QB, int npa, int cg, int kchunks, int stages,
-                                              int a_stream, int k) {
+                                              int a_stream, int k, int extra, int kr, int nbm) {
   GemmSmem s;
   s.a_off = 0;
   s.a_bytes = a_stream ? 0u : (uint32_t)(npa * kchunks * GT_ACHUNK);
-  s.stage_off = s.a_off + s.a_bytes;
-  s.stage_bytes = (uint32_t)(npa * (GT_BCHUNK + (a_stream ? GT_ACHUNK : 0)));
+  s.ax_off = s.a_off + s.a_bytes;
+  s.stage_off = s.ax_off + (extra ? (uint32_t)GT_AX : 0u);
+  // stage: B hi [, B lo] [, A hi [, A lo]] [, |b|^2 pieces]
+  s.stage_bytes = (uint32_t)(npa * (GT_BCHUNK + (a_stream ? GT_ACHUNK : 0)) +
+                             (extra ? GT_XCHUNK : 0));
   s.heap_off = s.stage_off + (uint32_t)stages * s.stage_bytes;
-  s.heap_bytes = (uint32_t)(cg * QB * k * 8);
-  s.nb_off = (s.heap_off + s.heap_bytes + 15u) & ~15u;
-  s.bar_off = s.nb_off + 4u * GT_BN * 4u;
+  s.heap_bytes = (uint32_t)((kr ? 1 : cg) * QB * k * 8);
+  s.sv_off = (s.heap_off + s.heap_bytes + 15u) & ~15u;
+  s.nb_off = s.sv_off + (kr ? (uint32_t)(4 * cg) * 16u * 32u * 4u : 0u);
+  s.fl_off = s.nb_off + (nbm == 0 ? 4u * GT_BN * 4u : 0u);
+  s.bar_off = s.fl_off + (uint32_t)(cg * QB * 8);
   // full[stages], empty[stages], a_full, a_empty, acc_full[2], acc_empty[2], aux
   s.total = s.bar_off + (uint32_t)(2 * stages + 7) * 8u + 16u;
   return s;
@@ -131,15 +148,28 @@ struct EpiState {
   float thr;       // score of floor (-inf when none): the fast rejection test
 };
 
-// One candidate against the heap, out of line (the slow path is rare); the
-// state travels by value so it stays in registers.
+// The slow path of 16 scores whose max reached the floor: each is offered
+// to the heap in a rolled loop.  Out of line, with the scores and the state
+// passed by value (registers), so the hot loop carries no call sites but one.
 template <int HS>
-__device__ __noinline__ EpiState heap_offer(uint64_t* heap, int k, uint64_t key, EpiState st) {
-  if (key > st.floor) {
-    heap_replace_root<HS>(heap, k, key);
-    uint64_t root = heap[0];
-    st.floor = root > st.gfl ? root : st.gfl;
-    st.thr = key_score(st.floor);
+__device__ __noinline__ EpiState epi_slow16(float v0, float v1, float v2, float v3, float v4,
+                                            float v5, float v6, float v7, float v8, float v9,
+                                            float v10, float v11, float v12, float v13,
+                                            float v14, float v15, int64_t col0, int64_t n_valid,
+                                            uint32_t id0, uint64_t* heap, int k, EpiState st) {
+  const float v[16] = {v0, v1, v2, v3, v4, v5, v6, v7, v8, v9, v10, v11, v12, v13, v14, v15};
+#pragma unroll 1
+  for (int j = 0; j < 16; ++j) {
+    const float vj = v[j];
+    if (vj >= st.thr && col0 + j < n_valid) {
+      const uint64_t key = make_key(vj, id0 + (uint32_t)j);
+      if (key > st.floor) {
+        heap_replace_root<HS>(heap, k, key);
+        const uint64_t root = heap[0];
+        st.floor = root > st.gfl ? root : st.gfl;
+        st.thr = key_score(st.floor);
+      }
+    }
   }
   return st;
 }
@@ -172,23 +202,38 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
+// A sorted list of the KR best keys in registers, ascending: key[0] is the
+// worst kept (0 while fewer than k are held); slots k .. KR-1 hold ~0 and
+// never change.  Inserts x (x > key[0]) with a branch-free network: each
+// slot takes its upper neighbour, x, or keeps its key.
+template <int KR>
+__device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    const uint64_t nxt = i + 1 < KR ? key[i + 1] : ~0ull;
+    const uint64_t cur = key[i];
+    key[i] = x > nxt ? nxt : (x > cur ? x : cur);
+  }
+}
+
 // 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
 // with one compare when their max is below the floor, else offer each.
-template <int HS>
+template <int HS, int NBM, int KR>
 __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const float* nbs,
                                           int64_t col0, const KnnGemmParams& p, bool row_on,
-                                          uint64_t* heap, EpiState& st) {
+                                          uint64_t* heap, uint64_t (&key)[KR > 0 ? KR : 1],
+                                          float* sv, EpiState& st) {
   float v[16];
-  const float4* nb4 = reinterpret_cast<const float4*>(nbs);
 #pragma unroll
-  for (int j4 = 0; j4 < 4; ++j4) {
-    float4 t = nb4[j4];
-    v[4 * j4 + 0] = __uint_as_float(r[o + 4 * j4 + 0]);
-    v[4 * j4 + 1] = __uint_as_float(r[o + 4 * j4 + 1]);
-    v[4 * j4 + 2] = __uint_as_float(r[o + 4 * j4 + 2]);
-    v[4 * j4 + 3] = __uint_as_float(r[o + 4 * j4 + 3]);
-    sub2(v[4 * j4 + 0], v[4 * j4 + 1], t.x, t.y);
-    sub2(v[4 * j4 + 2], v[4 * j4 + 3], t.z, t.w);
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[o + j]);
+  if (NBM == 0) {
+    const float4* nb4 = reinterpret_cast<const float4*>(nbs);
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      float4 t = nb4[j4];
+      sub2(v[4 * j4 + 0], v[4 * j4 + 1], t.x, t.y);
+      sub2(v[4 * j4 + 2], v[4 * j4 + 3], t.z, t.w);
+    }
   }
   float m0 = max3(v[0], v[1], v[2]);
   float m1 = max3(v[3], v[4], v[5]);
@@ -196,21 +241,56 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const 
   float m3 = max3(v[9], v[10], v[11]);
   float m4 = max3(v[12], v[13], v[14]);
   float mx = max3(max3(m0, m1, m2), max3(m3, m4, v[15]), -INFINITY);
-  if (mx >= st.thr && row_on) {
+  if constexpr (KR == 0) {
+    if (mx >= st.thr && row_on)
+      st = epi_slow16<HS>(v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], v[10],
+                          v[11], v[12], v[13], v[14], v[15], col0, p.n_valid,
+                          (uint32_t)(p.id_offset + col0), heap, p.k, st);
+  } else {
+    // warp-uniform slow path: each lane marks its scores at or above its
+    // floor in a 16-bit mask; the scores go through this warp's shared
+    // column (sv, stride 32), and the warp loops only while some lane still
+    // has marked scores (usually once or twice, not 16 times)
+    const bool mine = row_on && mx >= st.thr;
+    if (__any_sync(0xffffffffu, mine)) {
+      uint32_t mask = 0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (v[j] >= st.thr && col0 + j < p.n_valid)
-        st = heap_offer<HS>(heap, p.k, make_key(v[j], (uint32_t)(p.id_offset + col0 + j)), st);
+      for (int j = 0; j < 16; ++j) {
+        sv[j * 32] = v[j];
+        mask |= (v[j] >= st.thr ? 1u : 0u) << j;
+      }
+      if (!mine) mask = 0;
+      if (col0 + 16 > p.n_valid) {
+        const int64_t valid = p.n_valid - col0;
+        mask &= valid <= 0 ? 0u : (valid >= 16 ? 0xFFFFu : ((1u << valid) - 1u));
+      }
+      __syncwarp();
+      const uint32_t id0 = (uint32_t)(p.id_offset + col0);
+      while (__any_sync(0xffffffffu, mask != 0)) {
+        if (mask) {
+          const int j = __ffs(mask) - 1;
+          mask &= mask - 1;
+          const float vj = sv[j * 32];
+          const uint64_t x = make_key(vj, id0 + (uint32_t)j);
+          if (x > st.floor) {
+            list_insert<KR>(key, x);
+            st.floor = key[0] > st.gfl ? key[0] : st.gfl;
+            st.thr = key_score(st.floor);
+          }
+        }
+      }
+      __syncwarp();
     }
   }
 }
 
-template <int QB, int NPASS, int CG>
+template <int QB, int NPASS, int CG, int NBM, int KR>
 __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     knn_gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                          const __grid_constant__ CUtensorMap tm_a_lo,
                          const __grid_constant__ CUtensorMap tm_b_hi,
-                         const __grid_constant__ CUtensorMap tm_b_lo, const KnnGemmParams p) {
+                         const __grid_constant__ CUtensorMap tm_b_lo,
+                         const __grid_constant__ CUtensorMap tm_b_x, const KnnGemmParams p) {
   using L = GemmLayout<QB, NPASS, CG>;
   constexpr int NPA = L::NPA;
   constexpr int HS = CG * QB;     // heap slot stride
@@ -222,11 +302,19 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
   // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const GemmSmem lay = gemm_smem(QB, NPA, CG, p.kchunks, p.stages, p.a_stream, p.k);
+  const GemmSmem lay =
+      gemm_smem(QB, NPA, CG, p.kchunks, p.stages, p.a_stream, p.k, p.extra, KR, NBM);
   uint8_t* a_res = smem + lay.a_off;
+  uint8_t* ax = smem + lay.ax_off;
+  // offset of the |b|^2 pieces inside a stage
+  const uint32_t x_in_stage =
+      (uint32_t)(NPA * (GT_BCHUNK + (p.a_stream ? GT_ACHUNK : 0)));
   uint8_t* stage_base = smem + lay.stage_off;
   uint64_t* heap_all = reinterpret_cast<uint64_t*>(smem + lay.heap_off);
   float* nb_all = reinterpret_cast<float*>(smem + lay.nb_off);
+  float* sv_all = reinterpret_cast<float*>(smem + lay.sv_off);
+  volatile unsigned long long* fl_all =
+      reinterpret_cast<volatile unsigned long long*>(smem + lay.fl_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + lay.bar_off);
   uint64_t* full = bars;
   uint64_t* empty = bars + p.stages;
@@ -254,9 +342,32 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  for (int i = threadIdx.x; i < CG * QB; i += blockDim.x) fl_all[i] = 0ull;
   if (warp == L::MMA) {
     tmem_alloc(tmem_slot, 2 * GT_BN);
     tmem_relinquish();
+    if (p.extra) {
+      // the query-side half of the extra K step: every row is
+      // [-2^15, -2^11, -1, 0 ...], which against a base row's pieces
+      // [x 2^7, y, z, 0 ...] of |b|^2 = x 2^22 + y 2^11 + z adds -|b|^2
+      // (exactly: every product and partial sum is an integer < 2^31).
+      // Stored in the 32-byte swizzled layout: the 16-byte half c of row r
+      // sits at half c ^ ((r >> 2) & 1).
+      const __half2 c01 = __floats2half2_rn(-32768.0f, -2048.0f);
+      const __half2 c23 = __floats2half2_rn(-1.0f, 0.0f);
+      uint4 data;
+      data.x = *reinterpret_cast<const uint32_t*>(&c01);
+      data.y = *reinterpret_cast<const uint32_t*>(&c23);
+      data.z = 0u;
+      data.w = 0u;
+      for (int r = lane; r < 128; r += 32) {
+        const int sw = (r >> 2) & 1;
+        uint4* row = reinterpret_cast<uint4*>(ax + r * 32);
+        row[sw] = data;
+        row[sw ^ 1] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_shared();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -268,6 +379,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_a_hi);
       tma_prefetch_desc(&tm_b_hi);
+      if (p.extra) tma_prefetch_desc(&tm_b_x);
       if (NPASS == 3) {
         tma_prefetch_desc(&tm_a_lo);
         tma_prefetch_desc(&tm_b_lo);
@@ -300,9 +412,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
               break;
             }
             uint8_t* st = stage_base + (size_t)stage * lay.stage_bytes;
-            mbar_arrive_expect_tx(&full[stage],
-                                  (uint32_t)(NPA * GT_BCHUNK) + (p.a_stream ? a_bytes : 0u));
+            const bool xk = p.extra && kc == 0;
+            mbar_arrive_expect_tx(&full[stage], (uint32_t)(NPA * GT_BCHUNK) +
+                                                    (p.a_stream ? a_bytes : 0u) +
+                                                    (xk ? (uint32_t)GT_XCHUNK : 0u));
             tma_load_2d(st, &tm_b_hi, &full[stage], kc * GT_KCH, t * GT_BN);
+            if (xk) tma_load_2d(st + x_in_stage, &tm_b_x, &full[stage], 0, t * GT_BN);
             if (NPASS == 3)
               tma_load_2d(st + GT_BCHUNK, &tm_b_lo, &full[stage], kc * GT_KCH, t * GT_BN);
             if (p.a_stream) {
@@ -369,9 +484,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
               a_hi = smem_u32(a_res) + (uint32_t)kc * GT_ACHUNK;
               a_lo = smem_u32(a_res) + (uint32_t)(p.kchunks + kc) * GT_ACHUNK;
             }
+            if (p.extra && kc == 0)
+              umma_f16_ss(d_tmem, sdesc_k32(smem_u32(ax)), sdesc_k32(b_hi + x_in_stage), IDESC,
+                          0u);
 #pragma unroll
             for (int kk = 0; kk < GT_KCH / 16; ++kk) {
-              const uint32_t acc_in = (kc | kk) != 0;
+              const uint32_t acc_in = (kc | kk) != 0 || p.extra;
               umma_f16_ss(d_tmem, sdesc_k128(a_hi + kk * 32), sdesc_k128(b_hi + kk * 32), IDESC,
                           acc_in);
               if (NPASS == 3) {
@@ -411,6 +529,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     const bool row_on = row < QB;
     uint64_t* heap = heap_all + ch * QB + (row_on ? row : 0);
     float* nbw = nb_all + warp * CW;  // this warp's per-row terms of the tile
+    float* sv = sv_all + warp * 512 + lane;
+    uint64_t key[KR > 0 ? KR : 1];    // register mode: the sorted list
     uint32_t acc = 0, acc_ph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
@@ -420,14 +540,45 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       const int t1 = (int)((int64_t)(split + 1) * p.tiles / p.splits);
       const int64_t q = (int64_t)qb * QB + row;
       const bool q_ok = row_on && q < p.nq;
-      if (row_on)
-        for (int s = 0; s < p.k; ++s) heap[s * HS] = 0;
+      // Start from the k best of the query block's latest finished unit (a
+      // min-heap as written): the heap is full from its first tile, so its
+      // root is a real floor and every improvement reaches the shared floor.
+      // Column group 1 only takes the floor (its heap would duplicate them).
+      const int ds = *reinterpret_cast<volatile int*>(p.done + qb);
+      __threadfence();
+      uint64_t inherited = 0;
+      if constexpr (KR > 0) {
+        const unsigned long long* src =
+            reinterpret_cast<const unsigned long long*>(p.partial) +
+            ((size_t)(ds > 0 ? ds - 1 : 0) * p.nq_pad + q) * p.k;
+#pragma unroll
+        for (int i = 0; i < KR; ++i) {
+          uint64_t v = ~0ull;
+          if (i < p.k) v = (row_on && ds > 0 && ch == 0) ? __ldcg(src + i) : 0ull;
+          key[i] = v;
+        }
+        if (row_on && ds > 0) inherited = __ldcg(src);
+      } else if (row_on) {
+        if (ds > 0) {
+          const uint64_t* src = p.partial + ((size_t)(ds - 1) * p.nq_pad + q) * p.k;
+          for (int s = 0; s < p.k; ++s) {
+            const uint64_t key = __ldcg(reinterpret_cast<const unsigned long long*>(src) + s);
+            if (ch == 0) heap[s * HS] = key;
+          }
+          inherited = __ldcg(reinterpret_cast<const unsigned long long*>(src));
+        } else if (ch == 0) {
+          for (int s = 0; s < p.k; ++s) heap[s * HS] = 0;
+        }
+        if (ch == 1)
+          for (int s = 0; s < p.k; ++s) heap[s * HS] = 0;
+      }
       EpiState st;
       st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q) : 0ull;
+      if (inherited > st.gfl) st.gfl = inherited;
       st.floor = st.gfl;
       st.thr = key_score(st.floor);
       float4 nbr[CW / 128];
-      if (t0 < t1) {
+      if (NBM == 0 && t0 < t1) {
 #pragma unroll
         for (int i = 0; i < CW / 128; ++i)
           nbr[i] = __ldg(reinterpret_cast<const float4*>(p.nb + (int64_t)t0 * GT_BN + ch * CW) +
@@ -435,11 +586,14 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       }
       for (int t = t0; t < t1; ++t) {
         // stage this tile's per-row terms, prefetch the next tile's
-        __syncwarp();
+        if (NBM == 0) {
+          __syncwarp();
 #pragma unroll
-        for (int i = 0; i < CW / 128; ++i) reinterpret_cast<float4*>(nbw)[lane + 32 * i] = nbr[i];
-        __syncwarp();
-        if (t + 1 < t1) {
+          for (int i = 0; i < CW / 128; ++i)
+            reinterpret_cast<float4*>(nbw)[lane + 32 * i] = nbr[i];
+          __syncwarp();
+        }
+        if (NBM == 0 && t + 1 < t1) {
 #pragma unroll
           for (int i = 0; i < CW / 128; ++i)
             nbr[i] = __ldg(
@@ -461,8 +615,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          epi_sub16<HS>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, st);
-          epi_sub16<HS>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, st);
+          epi_sub16<HS, NBM, KR>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
           __syncwarp();
           tmem_wait_ld_regs(rb);
           if (c + 2 < NCH) {
@@ -472,8 +626,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
-          epi_sub16<HS>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, st);
-          epi_sub16<HS>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, st);
+          epi_sub16<HS, NBM, KR>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
           if (c + 2 < NCH) {
             __syncwarp();
             tmem_wait_ld_regs(ra);
@@ -481,8 +635,18 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         }
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;
+        if (CG == 2 && row_on) {
+          // the other column group's floor for this query (a tile old at most)
+          const uint64_t mine = KR > 0 ? key[0] : heap[0];
+          fl_all[ch * QB + row] = mine;
+          const uint64_t theirs = fl_all[(ch ^ 1) * QB + row];
+          if (theirs > st.floor) {
+            st.floor = theirs;
+            st.thr = key_score(theirs);
+          }
+        }
         if (q_ok && ((t - t0) & (GT_SHARE_TILES - 1)) == GT_SHARE_TILES - 1) {
-          const uint64_t root = heap[0];
+          const uint64_t root = KR > 0 ? key[0] : heap[0];
           uint64_t g;
           if (root != 0) {
             g = atomicMax(p.gfloor + q, (unsigned long long)root);
@@ -501,27 +665,54 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       }
       if (!ok) break;
       if (CG == 2) {
-        // the two column groups of each query meet: group 1's heap goes into
-        // group 0's, which is written out as the unit's list for the query
+        // the two column groups of each query meet: group 1's keys go into
+        // group 0's selection, which is written out as the unit's list
+        if constexpr (KR > 0) {
+          if (ch == 1 && row_on) {
+#pragma unroll
+            for (int i = 0; i < KR; ++i)
+              if (i < p.k) heap_all[i * QB + row] = key[i];
+          }
+        }
         asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
         if (ch == 0 && row_on) {
-          const uint64_t* other = heap + QB;
-          for (int s = 0; s < p.k; ++s) {
-            const uint64_t key = other[s * HS];
-            if (key > heap[0]) heap_replace_root<HS>(heap, p.k, key);
+          if constexpr (KR > 0) {
+#pragma unroll 1
+            for (int i = 0; i < p.k; ++i) {
+              const uint64_t x = heap_all[i * QB + row];
+              if (x > key[0]) list_insert<KR>(key, x);
+            }
+          } else {
+            const uint64_t* other = heap + QB;
+            for (int s = 0; s < p.k; ++s) {
+              const uint64_t kx = other[s * HS];
+              if (kx > heap[0]) heap_replace_root<HS>(heap, p.k, kx);
+            }
           }
         }
       }
-      if (ch == 0 && row_on) {
-        uint64_t* out = p.partial + ((size_t)split * p.nq_pad + q) * p.k;
-        for (int s = 0; s < p.k; ++s) {
-          uint64_t key = heap[s * HS];
-          if (key != 0 && p.out_scale != 1.0f)
-            key = make_key(key_score(key) * p.out_scale, ~(uint32_t)key);
-          out[s] = key;
+      if (ch == 0) {
+        if (row_on) {
+          uint64_t* out = p.partial + ((size_t)split * p.nq_pad + q) * p.k;
+          if constexpr (KR > 0) {
+#pragma unroll
+            for (int i = 0; i < KR; ++i)
+              if (i < p.k) out[i] = key[i];
+          } else {
+            for (int s = 0; s < p.k; ++s) out[s] = heap[s * HS];
+          }
+          __threadfence();
         }
+        // all of group 0's lists are out: mark the split finished
+        asm volatile("bar.sync %0, %1;" ::"r"(5), "r"(L::ROW_GROUPS * 32) : "memory");
+        if (warp == 0 && lane == 0) atomicMax(p.done + qb, split + 1);
       }
-      if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+      if (CG == 2) {
+        // floors are per query: clear this one before the partner can start
+        // the next unit and read it
+        if (row_on) fl_all[ch * QB + row] = 0ull;
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+      }
     }
     if (!ok) {
       *abort_flag = 1;

@@ -19,6 +19,10 @@ namespace mlxvs_b200 {
 // flags[1] collects max |y * mul| as float bits (to choose the scale).
 // norm_out[row] = sum(x^2) * norm_scale (float32; |b|^2 of src/knn.cpp:115
 // or |q|^2 of :123), or 0 when norm_scale == 0; padding rows get pad_norm.
+// xp (L2 base rows, may be null): |b|^2 as three fp16 pieces
+// [x 2^7, y, z, 0 x 13] with |b|^2 = x 2^22 + y 2^11 + z, the operand of the
+// GEMM's extra K step; fold_flag |= 1 when some |b|^2 is not an integer below
+// 2^31 (then the pieces are unusable and the epilogue subtracts norm_out).
 // ---------------------------------------------------------------------------
 struct PrepParams {
   const float* x;
@@ -35,6 +39,8 @@ struct PrepParams {
   float norm_scale;
   float pad_norm;
   uint32_t* flags;
+  __half* xp;
+  uint32_t* fold_flag;
 };
 
 #ifdef __CUDACC__
@@ -43,6 +49,27 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Lane 0 writes the 32-byte |b|^2 pieces of one row (zeros for padding rows).
+__device__ __forceinline__ uint32_t write_pieces(__half* xp, int64_t row, float ss, bool valid) {
+  uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)row * 16);
+  uint32_t bad = 0;
+  uint4 lo = make_uint4(0u, 0u, 0u, 0u);
+  if (valid) {
+    if (!(ss == rintf(ss) && ss >= 0.0f && ss < 2147483648.0f)) {
+      bad = 1;
+    } else {
+      const uint32_t u = (uint32_t)ss;
+      const __half2 xy = __floats2half2_rn((float)((u >> 22) << 7), (float)((u >> 11) & 2047u));
+      const __half2 z0 = __floats2half2_rn((float)(u & 2047u), 0.0f);
+      lo.x = *reinterpret_cast<const uint32_t*>(&xy);
+      lo.y = *reinterpret_cast<const uint32_t*>(&z0);
+    }
+  }
+  dst[0] = lo;
+  dst[1] = make_uint4(0u, 0u, 0u, 0u);
+  return bad;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -54,7 +81,7 @@ __device__ __forceinline__ float warp_max(float v) {
 __global__ void prep_rows_kernel(const PrepParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  uint32_t inexact = 0;
+  uint32_t inexact = 0, unfoldable = 0;
   float amax = 0.0f;
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
        row += warps) {
@@ -66,6 +93,7 @@ __global__ void prep_rows_kernel(const PrepParams p) {
         if (lrow) lrow[c] = __float2half_rn(0.0f);
       }
       if (p.norm_out && lane == 0) p.norm_out[row] = p.pad_norm;
+      if (p.xp && lane == 0) write_pieces(p.xp, row, 0.0f, false);
       continue;
     }
     const float* xr = p.x + (size_t)row * p.d;
@@ -107,7 +135,9 @@ __global__ void prep_rows_kernel(const PrepParams p) {
       }
     }
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
+    if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
   }
+  if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {
     inexact = __any_sync(0xffffffffu, inexact);
     amax = warp_max(amax);
@@ -123,7 +153,7 @@ __global__ void prep_rows_kernel(const PrepParams p) {
 __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  uint32_t inexact = 0;
+  uint32_t inexact = 0, unfoldable = 0;
   float amax = 0.0f;
   const int d4 = p.d >> 2;
   const int dp4 = p.d_pad >> 2;
@@ -133,6 +163,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
     if (row >= p.n) {
       for (int c = lane; c < dp4; c += 32) hrow[c] = make_uint2(0u, 0u);
       if (p.norm_out && lane == 0) p.norm_out[row] = p.pad_norm;
+      if (p.xp && lane == 0) write_pieces(p.xp, row, 0.0f, false);
       continue;
     }
     const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)row * p.d);
@@ -157,7 +188,9 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
     }
     ss = warp_sum(ss);
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
+    if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
   }
+  if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {
     inexact = __any_sync(0xffffffffu, inexact);
     amax = warp_max(amax);
@@ -186,15 +219,18 @@ __global__ void row_sumsq_kernel(const float* x, int64_t n, int32_t d, float* ou
 }
 
 // ---------------------------------------------------------------------------
-// merge_keys: for each query, the best k of num_lists lists of k keys
-// (list l, query q at lists[(l * list_rows + q) * k]), best first; then the
-// output as keys and / or ids + distances of the given kind:
+// merge_keys: for each query, the best k distinct keys of num_lists lists of
+// k keys (list l, query q at lists[(l * list_rows + q) * k]), best first;
+// scores are multiplied by `scale` (a power of two: the order is kept).
+// Output as keys and / or ids + distances of the given kind:
 //   kind 1 (L2)      distance max(qq[q] - score, 0), +inf where missing
 //                    (src/knn.cpp:122-131)
 //   kind 0, 2        distance = score, -inf where missing
 //   kind 3 (Hamming) distance = -score, +inf where missing
 // One CTA per query: candidates are sorted in shared memory with a bitonic
-// network, in rounds of MERGE_CAP - k new keys while more remain.
+// network, in rounds of cap - k new keys while more remain; after each round
+// warp 0 keeps the first k distinct keys (a key can sit in two lists when a
+// unit started from another unit's list).
 // ---------------------------------------------------------------------------
 constexpr int MERGE_THREADS = 256;
 constexpr int MERGE_CAP = 4096;
@@ -203,27 +239,27 @@ __global__ void __launch_bounds__(MERGE_THREADS)
     merge_keys_kernel(const uint64_t* __restrict__ lists, int32_t num_lists, int64_t list_rows,
                       int64_t nq, int32_t k, int32_t kind, const float* __restrict__ qq,
                       uint64_t* __restrict__ out_keys, int32_t* __restrict__ ids,
-                      float* __restrict__ dist, int32_t cap) {
+                      float* __restrict__ dist, int32_t cap, float scale) {
   extern __shared__ uint64_t buf[];  // [cap], a power of two > k
+  __shared__ int kept_s;
   const int64_t q = blockIdx.x;
   if (q >= nq) return;
   const int tid = threadIdx.x;
   const int64_t total = (int64_t)num_lists * k;
-  int64_t next = 0;    // candidates consumed
-  int kept = 0;        // valid sorted entries at the front of buf
-  while (next < total || next == 0) {
+  int64_t next = 0;  // candidates consumed
+  int kept = 0;      // distinct sorted keys at the front of buf
+  for (;;) {
     const int64_t room = cap - kept;
     const int64_t take = total - next < room ? total - next : room;
-    int count = kept + (int)take;
-    int size = 1;
+    const int count = kept + (int)take;
+    int size = 2;
     while (size < count) size <<= 1;
-    if (size < 2) size = 2;
     for (int i = tid; i < size; i += MERGE_THREADS) {
       if (i >= kept) {
-        int64_t c = next + (i - kept);
         uint64_t key = 0;
         if (i < count) {
-          int64_t l = c / k, j = c - l * k;
+          const int64_t c = next + (i - kept);
+          const int64_t l = c / k, j = c - l * k;
           key = lists[((size_t)l * list_rows + q) * k + j];
         }
         buf[i] = key;
@@ -233,10 +269,10 @@ __global__ void __launch_bounds__(MERGE_THREADS)
     for (int s2 = 2; s2 <= size; s2 <<= 1) {
       for (int stride = s2 >> 1; stride > 0; stride >>= 1) {
         for (int i = tid; i < size; i += MERGE_THREADS) {
-          int j = i ^ stride;
+          const int j = i ^ stride;
           if (j > i) {
-            uint64_t a = buf[i], b = buf[j];
-            bool desc = (i & s2) == 0;
+            const uint64_t a = buf[i], b = buf[j];
+            const bool desc = (i & s2) == 0;
             if (desc ? (a < b) : (a > b)) {
               buf[i] = b;
               buf[j] = a;
@@ -246,23 +282,41 @@ __global__ void __launch_bounds__(MERGE_THREADS)
         __syncthreads();
       }
     }
+    // compact the first k distinct non-empty keys to the front (in place:
+    // an element moves only left, and only to where nothing is read later)
+    if (tid < 32) {
+      int w = 0;
+      for (int base = 0; base < count && w < k; base += 32) {
+        const int i = base + tid;
+        const uint64_t key = i < count ? buf[i] : 0ull;
+        const bool keep = key != 0 && (i == 0 || buf[i - 1] != key);
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        __syncwarp();
+        const int pos = w + __popc(m & ((1u << tid) - 1u));
+        if (keep && pos < k) buf[pos] = key;
+        __syncwarp();
+        w += __popc(m);
+      }
+      if (tid == 0) kept_s = w < k ? w : k;
+    }
+    __syncthreads();
+    kept = kept_s;
     next += take;
-    kept = k < count ? k : count;
     if (next >= total) break;
   }
-  float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
+  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
   for (int j = tid; j < k; j += MERGE_THREADS) {
     uint64_t key = j < kept ? buf[j] : 0ull;
+    const float s = key_score(key) * scale;
+    if (key != 0 && scale != 1.0f) key = make_key(s, ~(uint32_t)key);
     if (out_keys) out_keys[(size_t)q * k + j] = key;
     if (ids) {
-      int32_t id = key_id(key);
+      const int32_t id = key_id(key);
       ids[(size_t)q * k + j] = id;
       if (dist) {
-        float s = key_score(key);
         float dv;
         if (kind == 1) {
-          float dd = qn - s;
-          dv = id >= 0 ? fmaxf(dd, 0.0f) : INFINITY;
+          dv = id >= 0 ? fmaxf(qn - s, 0.0f) : INFINITY;
         } else if (kind == 3) {
           dv = id >= 0 ? -s : INFINITY;
         } else {
