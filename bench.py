@@ -56,7 +56,8 @@ METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pi
 # DRAM bytes per launch of the dominant kernel, from the committed ncu
 # summaries under profiles/ (None until captured for that workload).
 NCU_TRAFFIC_PER_LAUNCH = {
-    "knn-l2-1m-k10": None,
+    # profiles/knn_gemm_topk_config1.md: 366.6 MB read + 14.1 MB written
+    "knn-l2-1m-k10": 380.7e6,
 }
 
 
