@@ -198,6 +198,39 @@ MLXVS_C_API int mlxvs_merge_keys_device(
 MLXVS_C_API int mlxvs_device_synchronize(void* stream);
 
 /**
+ * Hamming k-NN for callers that cannot allocate device memory.  No
+ * counterpart in the reference: it is mlxvs_hamming_knn_device with every
+ * scratch buffer placed in one 16 MiB array that the library reserves
+ * statically on each GPU that loads it (held until the process exits), so
+ * the call itself never calls cudaMalloc, cudaFree or any allocating
+ * routine.  Some callers cannot allocate: a serving loop that may not stall
+ * other streams (cudaMalloc and cudaFree synchronize the device), a host
+ * framework that has already reserved the device's memory for its own
+ * allocator, or code that promises a fixed memory footprint after start-up.
+ *
+ * Limits: bytes must be 16, 32, 64, 128, 256 or 512 (codes are read in
+ * place, so no padded copy is made) and rows / queries 16-byte aligned; the
+ * lists for nq * k must fit the array (about (k + 1) * nq * 8 bytes per base
+ * range; requests that do not fit even one range fail with
+ * MLXVS_ERROR_INVALID_ARGUMENT).  rows, queries, ids and distances are
+ * device pointers the caller owns.  The first call on a device looks the
+ * array up with cudaGetSymbolAddress and should come before any stream
+ * capture.  Every call reuses the same array, so calls that overlap on the
+ * GPU (other streams, other host threads, the same device) race; the call
+ * waits for its stream before returning and reports a kernel that gave up.
+ */
+MLXVS_C_API int mlxvs_hamming_knn_noalloc(
+    const uint8_t* rows,
+    int64_t n,
+    const uint8_t* queries,
+    int64_t nq,
+    int32_t bytes,
+    int32_t k,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
+/**
  * Benchmark support (not in the reference): when on, every launch of this
  * library's kernels is bracketed by CUDA events on its stream.  Turning it
  * on or off clears the records.

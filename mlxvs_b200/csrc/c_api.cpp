@@ -217,6 +217,15 @@ int mlxvs_merge_keys_device(const uint64_t* lists, int32_t num_lists, int64_t nq
   });
 }
 
+int mlxvs_hamming_knn_noalloc(const uint8_t* rows, int64_t n, const uint8_t* queries,
+                              int64_t nq, int32_t bytes, int32_t k, int32_t* ids,
+                              float* distances, void* stream) {
+  return guarded([&] {
+    mlxvs_b200::hamming_knn_noalloc(rows, n, queries, nq, bytes, k, ids, distances,
+                                    static_cast<cudaStream_t>(stream));
+  });
+}
+
 int mlxvs_profile_enable(int32_t on) {
   return guarded([&] { mlxvs_b200::profile_enable(on != 0); });
 }

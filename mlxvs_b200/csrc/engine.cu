@@ -650,3 +650,168 @@ void profile_read(const char* name, double* total_ms, int64_t* launches) {
 const char* version() { return MLXVS_B200_VERSION; }
 
 }  // namespace mlxvs_b200
+
+// ------------------------------------------------------ no-allocation entry
+// Hamming k-NN for callers that must not allocate device memory.  Its
+// scratch (the units' partial lists, the shared floors and an error word)
+// is the file-scope array below, which every GPU that loads this library
+// holds until the process exits; no call here allocates or frees.
+namespace mlxvs_b200 {
+
+namespace {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+struct NoAllocDevice {
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  int sms = 0;
+  int max_smem = 0;
+};
+
+// Set-up, once per device with that device current: the array's device
+// address (host code cannot use the symbol itself) and the device limits.
+const NoAllocDevice& noalloc_device() {
+  static std::mutex mu;
+  static NoAllocDevice devs[64];
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> guard(mu);
+  NoAllocDevice& d = devs[dev];
+  if (d.scratch == nullptr) {
+    int major = 0;
+    CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10)
+      throw std::runtime_error("[mlxvs_b200] needs an sm_100 GPU (B200)");
+    CK(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      throw std::runtime_error(std::string("[mlxvs_b200] cudaGetSymbolAddress failed: ") +
+                               cudaGetErrorString(e));
+    }
+    d.scratch = static_cast<unsigned char*>(p);
+  }
+  return d;
+}
+
+template <int V, int QH>
+void noalloc_hamming_launch(HammingParams p, const NoAllocDevice& dev, size_t list_room,
+                            int32_t* ids, float* dist, cudaStream_t s) {
+  auto kern = hamming_topk_kernel<V, QH>;
+  int stages = 4;
+  uint32_t smem = hamming_smem_bytes(V, QH, p.k, stages);
+  while (smem > (uint32_t)dev.max_smem && stages > 2)
+    smem = hamming_smem_bytes(V, QH, p.k, --stages);
+  if (smem > (uint32_t)dev.max_smem)
+    throw std::runtime_error("[mlxvs_b200] hamming: no kernel shape fits shared memory");
+  p.stages = stages;
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 1;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, QH + 32, smem));
+  const int slots = dev.sms * std::max(per_sm, 1);
+  // as many base ranges per query block as the scratch holds lists for
+  const size_t per_split = (size_t)p.nq_pad * p.k * 8;
+  const int fit = (int)std::min<size_t>(64, list_room / per_split);
+  p.splits = std::min(choose_splits(p.qblocks, p.tiles, slots, 2.0, 64), fit);
+  p.units = p.qblocks * p.splits;
+  kern<<<std::min(p.units, slots), QH + 32, smem, s>>>(p);
+  CK(cudaGetLastError());
+  launch_merge(p.partial, p.splits, p.nq_pad, p.nq, p.k, KIND_HAMMING, nullptr, nullptr, ids,
+               dist, s);
+}
+
+}  // namespace
+
+void hamming_knn_noalloc(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
+                         int bytes, int k, int32_t* ids, float* dist, cudaStream_t s) {
+  const char* op = "[mlxvs::hamming_knn_noalloc] ";
+  require(ids != nullptr || nq == 0, std::string(op) + "ids must not be NULL.");
+  require(k >= 1 && k <= 256, std::string(op) + "k must be in [1, 256].");
+  require(n >= 0 && n < (1LL << 31), std::string(op) + "the number of rows must be in [0, 2^31).");
+  require(nq >= 0 && nq < (1LL << 31),
+          std::string(op) + "the number of queries must be in [0, 2^31).");
+  int V = 0;
+  for (int v = 1; v <= 32; v <<= 1)
+    if (16 * v == bytes) V = v;
+  require(V != 0, std::string(op) +
+                      "bytes must be 16, 32, 64, 128, 256 or 512: the codes are read in place "
+                      "(a padded copy would need an allocation).");
+  require((rows == nullptr || (reinterpret_cast<uintptr_t>(rows) & 15) == 0) &&
+              (queries == nullptr || (reinterpret_cast<uintptr_t>(queries) & 15) == 0),
+          std::string(op) + "rows and queries must be 16-byte aligned.");
+  const NoAllocDevice& dev = noalloc_device();
+  if (nq == 0) return;
+  if (n == 0) {
+    launch_fill(nq * k, KIND_HAMMING, ids, dist, nullptr, s);
+    return;
+  }
+  require(rows != nullptr && queries != nullptr, std::string(op) + "null input.");
+  int QH = 256;
+  while (QH > 64 && (uint32_t)QH * k * 8u > 64u * 1024u) QH >>= 1;
+  if (V > 16 && QH > 128) QH = 128;
+  const int64_t nq_pad = round_up(nq, QH);
+  // scratch layout: error word | shared floors [nq_pad] | lists [splits][nq_pad][k]
+  const size_t floors_off = 256;
+  const size_t lists_off = (size_t)round_up(floors_off + (size_t)nq_pad * 8, 256);
+  const size_t one_split = (size_t)nq_pad * k * 8;
+  if (lists_off + one_split > NOALLOC_SCRATCH_BYTES)
+    throw std::invalid_argument(
+        std::string(op) + "nq * k is too large for the 16 MiB static scratch: it needs " +
+        std::to_string(lists_off + one_split) + " bytes (at most about 2^21 / (k + 1) queries).");
+  HammingParams p{};
+  p.rows = rows;
+  p.queries = queries;
+  p.n = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.qblocks = (int)(nq_pad / QH);
+  p.tiles = (int)((n + HM_HT - 1) / HM_HT);
+  p.k = k;
+  p.id_offset = 0;
+  p.err = reinterpret_cast<uint32_t*>(dev.scratch);
+  p.wait_ns = WAIT_LIMIT_NS;
+  p.gfloor = reinterpret_cast<unsigned long long*>(dev.scratch + floors_off);
+  p.partial = reinterpret_cast<uint64_t*>(dev.scratch + lists_off);
+  // the array keeps the previous call's contents: clear the error word and
+  // the floors, which must start at zero (every list slot is rewritten)
+  CK(cudaMemsetAsync(dev.scratch, 0, lists_off, s));
+  const size_t room = NOALLOC_SCRATCH_BYTES - lists_off;
+  switch (V) {
+#define MLXVS_NOALLOC_V(V_)                                                   \
+  case V_:                                                                    \
+    if (QH == 256) noalloc_hamming_launch<V_, 256>(p, dev, room, ids, dist, s); \
+    else if (QH == 128) noalloc_hamming_launch<V_, 128>(p, dev, room, ids, dist, s); \
+    else noalloc_hamming_launch<V_, 64>(p, dev, room, ids, dist, s);        \
+    break;
+    MLXVS_NOALLOC_V(1)
+    MLXVS_NOALLOC_V(2)
+    MLXVS_NOALLOC_V(4)
+#undef MLXVS_NOALLOC_V
+    case 8:
+      if (QH == 256) noalloc_hamming_launch<8, 256>(p, dev, room, ids, dist, s);
+      else if (QH == 128) noalloc_hamming_launch<8, 128>(p, dev, room, ids, dist, s);
+      else noalloc_hamming_launch<8, 64>(p, dev, room, ids, dist, s);
+      break;
+    case 16:
+      if (QH == 256) noalloc_hamming_launch<16, 256>(p, dev, room, ids, dist, s);
+      else if (QH == 128) noalloc_hamming_launch<16, 128>(p, dev, room, ids, dist, s);
+      else noalloc_hamming_launch<16, 64>(p, dev, room, ids, dist, s);
+      break;
+    default:
+      if (QH == 128) noalloc_hamming_launch<32, 128>(p, dev, room, ids, dist, s);
+      else noalloc_hamming_launch<32, 64>(p, dev, room, ids, dist, s);
+      break;
+  }
+  // report a kernel that gave up waiting: the call returns after its work
+  uint32_t err = 0;
+  CK(cudaMemcpyAsync(&err, dev.scratch, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (err != 0)
+    throw std::runtime_error("[mlxvs_b200] a kernel gave up waiting (error word " +
+                             std::to_string(err) + ")");
+}
+
+}  // namespace mlxvs_b200

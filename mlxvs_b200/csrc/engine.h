@@ -58,6 +58,13 @@ void profile_enable(bool on);
  * "fill"), or of all of them when name is null.  Waits for the events. */
 void profile_read(const char* name, double* total_ms, int64_t* launches);
 
+/** Hamming k-NN with no device allocation: its scratch is a 16 MiB static
+ * device array shared by all calls (they race if they overlap on the GPU).
+ * Codes must be 16, 32, 64, 128, 256 or 512 bytes and 16-byte aligned. The
+ * first call on a device looks the array up.  Waits for its stream. */
+void hamming_knn_noalloc(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
+                         int bytes, int k, int32_t* ids, float* dist, cudaStream_t s);
+
 /** Version string. */
 const char* version();
 
