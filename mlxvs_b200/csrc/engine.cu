@@ -210,6 +210,24 @@ void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64
                   cudaStream_t s, float scale = 1.0f) {
   if (nq == 0) return;
   int64_t total = (int64_t)num_lists * k;
+  if (k <= 32 && total <= 32 * 32) {
+    ProfScope prof("merge", s);
+    const unsigned blocks = (unsigned)((nq + 7) / 8);
+#define MLXVS_MERGE_WARP(M_)                                                            \
+  merge_keys_warp_kernel<M_><<<blocks, 256, 0, s>>>(lists, num_lists, list_rows, nq, k, \
+                                                     kind, qq, out_keys, ids, dist, scale)
+    if (total <= 32 * 4)
+      MLXVS_MERGE_WARP(4);
+    else if (total <= 32 * 8)
+      MLXVS_MERGE_WARP(8);
+    else if (total <= 32 * 16)
+      MLXVS_MERGE_WARP(16);
+    else
+      MLXVS_MERGE_WARP(32);
+#undef MLXVS_MERGE_WARP
+    CK(cudaGetLastError());
+    return;
+  }
   int cap = 2;
   while (cap < total && cap < MERGE_CAP) cap <<= 1;
   while (cap <= k) cap <<= 1;
@@ -344,7 +362,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   int QB = 0, CG = 0, KR = 0, stages = 0, a_stream = 0;
   const int want_stages = exact ? 4 : 2;
   // k <= 16 keeps each query's list in registers (two column groups)
-  const int kr = k <= 8 ? 8 : (k <= 16 ? 16 : 0);
+  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : 0));
   struct Shape { int qb, cg, kr, min_st; };
   const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, 0, want_stages},
                          {128, 1, 0, want_stages},  {64, 1, 0, want_stages},
@@ -425,6 +443,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
       launch_gemm<QB_, 3, CG_, 0, KR_>(maps, p, grid, smem, s);           \
   }
   MLXVS_GEMM(128, 2, 8)
+  MLXVS_GEMM(128, 2, 12)
   MLXVS_GEMM(128, 2, 16)
   MLXVS_GEMM(128, 2, 0)
   MLXVS_GEMM(128, 1, 0)

@@ -208,11 +208,15 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // slot takes its upper neighbour, x, or keeps its key.
 template <int KR>
 __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
+  // b[i] = x beats key[i]; slot i then takes key[i + 1] when x also beats
+  // that one, else x (one compare per slot, shared by its two neighbours)
+  bool b[KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) b[i] = x > key[i];
 #pragma unroll
   for (int i = 0; i < KR; ++i) {
-    const uint64_t nxt = i + 1 < KR ? key[i + 1] : ~0ull;
-    const uint64_t cur = key[i];
-    key[i] = x > nxt ? nxt : (x > cur ? x : cur);
+    const bool up = i + 1 < KR ? b[i + 1] : false;
+    key[i] = up ? key[i + 1] : (b[i] ? x : key[i]);
   }
 }
 

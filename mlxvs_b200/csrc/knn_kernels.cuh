@@ -328,6 +328,69 @@ __global__ void __launch_bounds__(MERGE_THREADS)
   }
 }
 
+// The same merge with one warp per query, for k <= 32 and at most 32 * MPL
+// candidates: every lane holds up to MPL candidates in registers; each of the
+// k rounds takes the warp's largest key (a shuffle max) and clears it from
+// every lane (so a key present in two lists is taken once).
+template <int MPL>
+__global__ void __launch_bounds__(256)
+    merge_keys_warp_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
+                           int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
+                           const float* __restrict__ qq, uint64_t* __restrict__ out_keys,
+                           int32_t* __restrict__ ids, float* __restrict__ dist, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t q = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (q >= nq) return;
+  const int total = num_lists * k;
+  uint64_t c[MPL];
+#pragma unroll
+  for (int m = 0; m < MPL; ++m) {
+    const int idx = m * 32 + lane;
+    uint64_t key = 0;
+    if (idx < total) {
+      const int l = idx / k, j = idx - l * k;
+      key = __ldg(reinterpret_cast<const unsigned long long*>(lists) +
+                  ((size_t)l * list_rows + q) * k + j);
+    }
+    c[m] = key;
+  }
+  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
+  for (int o = 0; o < k; ++o) {
+    uint64_t best = c[0];
+#pragma unroll
+    for (int m = 1; m < MPL; ++m) best = c[m] > best ? c[m] : best;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, off);
+      best = other > best ? other : best;
+    }
+#pragma unroll
+    for (int m = 0; m < MPL; ++m)
+      if (c[m] == best) c[m] = 0;
+    if (lane == (o & 31)) {
+      uint64_t key = best;
+      const float sc = key_score(key) * scale;
+      if (key != 0 && scale != 1.0f) key = make_key(sc, ~(uint32_t)key);
+      if (out_keys) out_keys[(size_t)q * k + o] = key;
+      if (ids) {
+        const int32_t id = key_id(key);
+        ids[(size_t)q * k + o] = id;
+        if (dist) {
+          float dv;
+          if (kind == 1) {
+            dv = id >= 0 ? fmaxf(qn - sc, 0.0f) : INFINITY;
+          } else if (kind == 3) {
+            dv = id >= 0 ? -sc : INFINITY;
+          } else {
+            dv = id >= 0 ? sc : -INFINITY;
+          }
+          dist[(size_t)q * k + o] = dv;
+        }
+      }
+    }
+  }
+}
+
 // Outputs of a search over no rows: every id -1, every distance missing.
 __global__ void fill_missing_kernel(int64_t count, int32_t kind, int32_t* ids, float* dist,
                                     uint64_t* keys) {

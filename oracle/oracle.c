@@ -113,14 +113,33 @@ static void knn_core(const float* base, int64_t n, const float* queries,
       nb[j] = ss;
     }
   }
+  /* tasks: (block of QBLK queries, chunk of base rows), enough of them to
+     keep every thread busy also when there are few queries; each task keeps
+     its own heaps, merged per query at the end */
   int64_t blocks = (nq + QBLK - 1) / QBLK;
+  int64_t chunks = 1;
+#ifdef _OPENMP
+  {
+    int64_t want = 4 * (int64_t)omp_get_max_threads();
+    chunks = (want + blocks - 1) / (blocks > 0 ? blocks : 1);
+    int64_t max_chunks = (n + RBLK - 1) / RBLK;
+    if (chunks > max_chunks) chunks = max_chunks;
+    if (chunks < 1) chunks = 1;
+  }
+#endif
+  const int64_t rows_per_chunk = ((n + chunks - 1) / chunks + RBLK - 1) / RBLK * RBLK;
+  uint64_t* task_heaps =
+      (uint64_t*)calloc((size_t)(blocks > 0 ? blocks : 1) * chunks * QBLK * k, sizeof(uint64_t));
 #pragma omp parallel for schedule(dynamic, 1)
-  for (int64_t blk = 0; blk < blocks; ++blk) {
+  for (int64_t task = 0; task < blocks * chunks; ++task) {
+    int64_t blk = task / chunks, ch = task % chunks;
     int64_t i0 = blk * QBLK;
     int64_t i1 = i0 + QBLK < nq ? i0 + QBLK : nq;
-    uint64_t* heaps = (uint64_t*)calloc((size_t)QBLK * (size_t)k, sizeof(uint64_t));
-    for (int64_t j0 = 0; j0 < n; j0 += RBLK) {
-      int64_t j1 = j0 + RBLK < n ? j0 + RBLK : n;
+    int64_t r0 = ch * rows_per_chunk;
+    int64_t r1 = r0 + rows_per_chunk < n ? r0 + rows_per_chunk : n;
+    uint64_t* heaps = task_heaps + (size_t)task * QBLK * k;
+    for (int64_t j0 = r0; j0 < r1; j0 += RBLK) {
+      int64_t j1 = j0 + RBLK < r1 ? j0 + RBLK : r1;
       for (int64_t i = i0; i < i1; ++i) {
         const float* qi = q + (size_t)i * d;
         uint64_t* h = heaps + (size_t)(i - i0) * k;
@@ -140,13 +159,21 @@ static void knn_core(const float* base, int64_t n, const float* queries,
         }
       }
     }
-    for (int64_t i = i0; i < i1; ++i) {
-      uint64_t* h = heaps + (size_t)(i - i0) * k;
-      qsort(h, (size_t)k, sizeof(uint64_t), cmp_desc);
-      memcpy(keys + (size_t)i * k, h, (size_t)k * sizeof(uint64_t));
-    }
-    free(heaps);
   }
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < nq; ++i) {
+    int64_t blk = i / QBLK;
+    uint64_t* h = (uint64_t*)calloc((size_t)k, sizeof(uint64_t));
+    for (int64_t ch = 0; ch < chunks; ++ch) {
+      const uint64_t* src = task_heaps + ((size_t)(blk * chunks + ch) * QBLK + (i - blk * QBLK)) * k;
+      for (int32_t j = 0; j < k; ++j)
+        if (src[j] > h[0]) heap_push(h, k, src[j]);
+    }
+    qsort(h, (size_t)k, sizeof(uint64_t), cmp_desc);
+    memcpy(keys + (size_t)i * k, h, (size_t)k * sizeof(uint64_t));
+    free(h);
+  }
+  free(task_heaps);
   free(nb);
   free(bu);
   free(qu);
@@ -237,13 +264,29 @@ int oracle_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries,
   if (k < 1 || k > 256 || bytes < 1 || n < 0 || nq < 0) return 1;
   int old = set_threads(threads);
   int64_t blocks = (nq + QBLK - 1) / QBLK;
+  int64_t chunks = 1;
+#ifdef _OPENMP
+  {
+    int64_t want = 4 * (int64_t)omp_get_max_threads();
+    chunks = (want + blocks - 1) / (blocks > 0 ? blocks : 1);
+    int64_t max_chunks = (n + RBLK - 1) / RBLK;
+    if (chunks > max_chunks) chunks = max_chunks;
+    if (chunks < 1) chunks = 1;
+  }
+#endif
+  const int64_t rows_per_chunk = ((n + chunks - 1) / chunks + RBLK - 1) / RBLK * RBLK;
+  uint64_t* task_heaps =
+      (uint64_t*)calloc((size_t)(blocks > 0 ? blocks : 1) * chunks * QBLK * k, sizeof(uint64_t));
 #pragma omp parallel for schedule(dynamic, 1)
-  for (int64_t blk = 0; blk < blocks; ++blk) {
+  for (int64_t task = 0; task < blocks * chunks; ++task) {
+    int64_t blk = task / chunks, ch = task % chunks;
     int64_t i0 = blk * QBLK;
     int64_t i1 = i0 + QBLK < nq ? i0 + QBLK : nq;
-    uint64_t* heaps = (uint64_t*)calloc((size_t)QBLK * (size_t)k, sizeof(uint64_t));
-    for (int64_t j0 = 0; j0 < n; j0 += RBLK) {
-      int64_t j1 = j0 + RBLK < n ? j0 + RBLK : n;
+    int64_t r0 = ch * rows_per_chunk;
+    int64_t r1 = r0 + rows_per_chunk < n ? r0 + rows_per_chunk : n;
+    uint64_t* heaps = task_heaps + (size_t)task * QBLK * k;
+    for (int64_t j0 = r0; j0 < r1; j0 += RBLK) {
+      int64_t j1 = j0 + RBLK < r1 ? j0 + RBLK : r1;
       for (int64_t i = i0; i < i1; ++i) {
         const uint8_t* qi = queries + (size_t)i * bytes;
         uint64_t* h = heaps + (size_t)(i - i0) * k;
@@ -255,18 +298,26 @@ int oracle_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries,
         }
       }
     }
-    for (int64_t i = i0; i < i1; ++i) {
-      uint64_t* h = heaps + (size_t)(i - i0) * k;
-      qsort(h, (size_t)k, sizeof(uint64_t), cmp_desc);
-      for (int32_t j = 0; j < k; ++j) {
-        int32_t id = key_id(h[j]);
-        ids[(size_t)i * k + j] = id;
-        if (distances)
-          distances[(size_t)i * k + j] = id >= 0 ? -key_score(h[j]) : INFINITY;
-      }
-    }
-    free(heaps);
   }
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < nq; ++i) {
+    int64_t blk = i / QBLK;
+    uint64_t* h = (uint64_t*)calloc((size_t)k, sizeof(uint64_t));
+    for (int64_t ch = 0; ch < chunks; ++ch) {
+      const uint64_t* src = task_heaps + ((size_t)(blk * chunks + ch) * QBLK + (i - blk * QBLK)) * k;
+      for (int32_t j = 0; j < k; ++j)
+        if (src[j] > h[0]) heap_push(h, k, src[j]);
+    }
+    qsort(h, (size_t)k, sizeof(uint64_t), cmp_desc);
+    for (int32_t j = 0; j < k; ++j) {
+      int32_t id = key_id(h[j]);
+      ids[(size_t)i * k + j] = id;
+      if (distances)
+        distances[(size_t)i * k + j] = id >= 0 ? -key_score(h[j]) : INFINITY;
+    }
+    free(h);
+  }
+  free(task_heaps);
   restore_threads(old);
   return 0;
 }
