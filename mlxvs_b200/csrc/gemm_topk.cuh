@@ -144,7 +144,7 @@ __device__ __forceinline__ void heap_replace_root(uint64_t* heap, int k, uint64_
 
 struct EpiState {
   uint64_t floor;  // no candidate at or below this key can be in the result
-  uint64_t gfl;    // last shared floor seen
+  uint64_t gfl;    // the shared floor as last read or raised by this thread
   float thr;       // score of floor (-inf when none): the fast rejection test
 };
 
@@ -166,7 +166,7 @@ __device__ __noinline__ EpiState epi_slow16(float v0, float v1, float v2, float 
       if (key > st.floor) {
         heap_replace_root<HS>(heap, k, key);
         const uint64_t root = heap[0];
-        st.floor = root > st.gfl ? root : st.gfl;
+        if (root > st.floor) st.floor = root;
         st.thr = key_score(st.floor);
       }
     }
@@ -278,7 +278,7 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const 
           const uint64_t x = make_key(vj, id0 + (uint32_t)j);
           if (x > st.floor) {
             list_insert<KR>(key, x);
-            st.floor = key[0] > st.gfl ? key[0] : st.gfl;
+            if (key[0] > st.floor) st.floor = key[0];
             st.thr = key_score(st.floor);
           }
         }
@@ -581,6 +581,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       if (inherited > st.gfl) st.gfl = inherited;
       st.floor = st.gfl;
       st.thr = key_score(st.floor);
+      uint64_t gnext = st.gfl;
       float4 nbr[CW / 128];
       if (NBM == 0 && t0 < t1) {
 #pragma unroll
@@ -650,14 +651,11 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
           }
         }
         if (q_ok && ((t - t0) & (GT_SHARE_TILES - 1)) == GT_SHARE_TILES - 1) {
-          const uint64_t root = KR > 0 ? key[0] : heap[0];
-          uint64_t g;
-          if (root != 0) {
-            g = atomicMax(p.gfloor + q, (unsigned long long)root);
-            if (root > g) g = root;
-          } else {
-            g = *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q);
-          }
+          // the shared floor loaded one tile ago (its latency is hidden
+          // behind this tile's work); then publish the best floor this
+          // thread knows if it beats the last shared one seen, and load the
+          // shared one for the next tile
+          const uint64_t g = gnext;
           if (g > st.gfl) {
             st.gfl = g;
             if (g > st.floor) {
@@ -665,6 +663,11 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
               st.thr = key_score(g);
             }
           }
+          if (st.floor > st.gfl) {
+            atomicMax(p.gfloor + q, (unsigned long long)st.floor);
+            st.gfl = st.floor;
+          }
+          gnext = *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q);
         }
       }
       if (!ok) break;

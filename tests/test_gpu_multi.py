@@ -1,0 +1,92 @@
+"""The row-sharded search on 2 GPUs of one node (NCCL, one process per GPU):
+results equal the single-GPU search (bit for bit on integer data, recall 1
+on float data, where each shard's operand scale may round a score
+differently).  Skipped on a box with fewer than 2 GPUs."""
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tests import data
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
+
+WORLD = 2
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+CASES = [("l2", 10, True), ("l2", 10, False), ("inner_product", 12, False), ("l2", 64, False)]
+
+
+def make_case(metric, integer):
+    if integer:
+        return data.gaussian_mixture_int(60_000, 128, 32, seed=41, nq=1_000)
+    b = data.normal_rows(60_000, 128, seed=42)
+    q = data.normal_rows(1_000, 128, seed=43)
+    b[:20_000] *= np.float32(2.5)  # the shards' operand scales differ
+    return b, q
+
+
+def _worker(rank, world, port, out):
+    import mlxvs_b200 as mv
+    from mlxvs_b200 import distributed as mvd
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        for metric, k, integer in CASES:
+            b, q = make_case(metric, integer)
+            bounds = mvd.shard_bounds(b.shape[0], world)
+            lo, hi = bounds[rank], bounds[rank + 1]
+            shard = torch.from_numpy(b[lo:hi]).to(dev)
+            tq = torch.from_numpy(q).to(dev)
+            first = mvd.sharded_brute_force_knn(shard, tq, k, metric, id_offset=lo)
+            ids, dist_ = mvd.sharded_brute_force_knn(shard, tq, k, metric, id_offset=lo)
+            mv.synchronize()
+            # every rank holds the same result, the same on every call
+            same = bool(torch.equal(ids, first[0]) and torch.equal(dist_, first[1]))
+            gathered = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(gathered, ids)
+            same = same and all(bool(torch.equal(g, ids)) for g in gathered)
+            single = None
+            if rank == 0:
+                sids, sdist = mv.brute_force_knn(torch.from_numpy(b).to(dev), tq, k, metric)
+                if integer:
+                    single = bool(torch.equal(ids, sids) and torch.equal(dist_, sdist))
+                else:
+                    scores = data.exact_scores(metric, q, b)
+                    single = data.recall(ids.cpu().numpy(), scores, k, tol=1e-4) == 1.0
+            out[(rank, metric, k, integer)] = (same, single)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD,
+                    reason="needs 2 GPUs")
+def test_two_gpus_match_single():
+    port = free_port()
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_worker, args=(WORLD, port, out), nprocs=WORLD, start_method="spawn",
+                           join=True)
+        res = dict(out)
+    for metric, k, integer in CASES:
+        for r in range(WORLD):
+            same, single = res[(r, metric, k, integer)]
+            assert same, (r, metric, k, integer)
+            if r == 0:
+                assert single, (metric, k, integer)
