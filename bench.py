@@ -45,6 +45,13 @@ WORKLOADS = {
     "knn-cos-1m-1536": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
                             metric="cosine", rank=64,
                             desc="config 2: 1M x 1536 fp32 unit rows, cosine, k=10"),
+    # the exact k-NN graph (all_neighbors, one cluster,
+    # brute force) of the config-1 generator's 1M rows, k=32 (the reference
+    # searches k + 1 = 33 and drops each row itself)
+    "allnn-l2-1m-k32": dict(kind="allnn", n=1_000_000, nq=1_000_000, d=128, k=32, metric="l2",
+                            clusters=1024,
+                            desc="config 3: all_neighbors of 1M x 128 fp32 (integer-valued "
+                                 "mixture), L2, k=32 self excluded"),
     # BASELINE config 4
     "hamming-10m-1024b": dict(kind="hamming", n=10_000_000, nq=10_000, bytes=128, k=10,
                               prototypes=4096, flip=0.1,
@@ -141,6 +148,9 @@ def gen_codes_torch(n, nbytes, prototypes, flip, seed, device):
 
 
 def make_inputs(w, device, seed=0):
+    if w["kind"] == "allnn":
+        base = gen_mixture_torch(w["n"], w["d"], w["clusters"], seed, device)
+        return base, base
     if w["kind"] == "knn":
         base = gen_mixture_torch(w["n"], w["d"], w["clusters"], seed, device)
         q = gen_mixture_torch(w["nq"], w["d"], w["clusters"], seed + 1, device)
@@ -227,6 +237,8 @@ def cpu_sample_rate(w, base_np, q_np, budget_s, threads=0):
         t = time.perf_counter()
         if w["kind"] == "hamming":
             O.hamming_knn(base_np, q_np[:m], w["k"], threads=threads)
+        elif w["kind"] == "allnn":
+            O.all_neighbors(base_np, w["k"], w["metric"], threads=threads, begin=0, end=m)
         else:
             O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"], threads=threads)
         return time.perf_counter() - t
@@ -262,6 +274,8 @@ def reference_arm(args, w, peaks):
     def step():
         if w["kind"] == "hamming":
             O.hamming_knn(base_np, q_np[:m], w["k"])
+        elif w["kind"] == "allnn":
+            O.all_neighbors(base_np, w["k"], w["metric"], begin=0, end=m)
         else:
             O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"])
 
@@ -273,6 +287,9 @@ def reference_arm(args, w, peaks):
     el = time.perf_counter() - t
     value = m * args.steps / el
     sample = f"{m} of {w['nq']} queries against all {w['n']} base rows per step"
+    if w["kind"] == "allnn":
+        sample = (f"the lists of {m} of {w['n']} rows per step (a k + 1 search against all "
+                  f"rows, then the row itself dropped)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -336,7 +353,10 @@ def main():
     base, q = make_inputs(w, dev)
     bounds = mvd.shard_bounds(w["n"], world)
     lo, hi = bounds[rank], bounds[rank + 1]
-    shard = base[lo:hi].contiguous()
+    is_allnn = w["kind"] == "allnn"
+    # all_neighbors splits the rows to list (queries) over the GPUs, each
+    # holding all rows; the others split the base rows
+    shard = base if is_allnn else base[lo:hi].contiguous()
     full_base = base
     k = w["k"]
     is_hamming = w["kind"] == "hamming"
@@ -344,6 +364,10 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        if is_allnn:
+            if world == 1:
+                return mv.all_neighbors(shard, k, metric, algo="brute_force")
+            return mv.all_neighbors_rows(shard, k, metric, begin=lo, end=hi)
         if world == 1:
             if is_hamming:
                 return mv.hamming_knn(shard, q, k)
@@ -387,6 +411,12 @@ def main():
 
     # a quick self-check of the last step's output on a few queries (rank 0)
     check = None
+    if rank == 0 and is_allnn:
+        from oracle import oracle as O
+
+        oids, odist = O.all_neighbors(full_base.cpu().numpy(), k, metric, begin=0, end=4)
+        check = bool(np.array_equal(ids[:4].cpu().numpy(), oids) and
+                     np.array_equal(dist_out[:4].cpu().numpy(), odist))
     if rank == 0 and not is_hamming and w["kind"] == "knn":
         from oracle import oracle as O
 
@@ -404,12 +434,17 @@ def main():
             bnp, qnp = base_h.numpy(), q_h.numpy()
 
             def e2e_step():
+                if is_allnn:
+                    return mv.all_neighbors(bnp, k, metric, algo="brute_force")
                 if is_hamming:
                     return mv.hamming_knn(bnp, qnp, k)
                 return mv.brute_force_knn(bnp, qnp, k, metric)
         else:
             def e2e_step():
                 sd = base_h.to(dev, non_blocking=True)
+                if is_allnn:
+                    i, d_ = mv.all_neighbors_rows(sd, k, metric, begin=lo, end=hi)
+                    return i.cpu(), d_.cpu()
                 qd = q_h.to(dev, non_blocking=True)
                 if is_hamming:
                     i, d_ = mvd.sharded_hamming_knn(sd, qd, k, id_offset=lo)
@@ -431,10 +466,16 @@ def main():
             e2e_s = float(t.item())
         h2d = shard.numel() * shard.element_size() + q.numel() * q.element_size()
         d2h = w["nq"] * k * 8
+        if is_allnn:  # the rows are the queries; this rank's lists come back
+            h2d = shard.numel() * shard.element_size()
+            d2h = (hi - lo) * k * 8
         e2e = {"value": w["nq"] * args.e2e_steps / e2e_s, "unit": "queries/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "steps": args.e2e_steps, "path": "mlxvs_brute_force_knn (C API, host buffers)"
                if world == 1 else "mlxvs_b200.distributed on pinned host buffers"}
+        if is_allnn:
+            e2e["path"] = ("mlxvs_all_neighbors (C API, host buffers)" if world == 1 else
+                           "mlxvs_all_neighbors_device per rank on pinned host buffers")
 
     # roofline of the dominant kernel (rank 0's launches)
     roof = None
@@ -453,6 +494,8 @@ def main():
                     "algorithmic_per_launch": f"{pops:.3e} 32-bit popcounts"}
         else:
             flops = 2.0 * w["nq"] * n_local * w["d"]
+            if is_allnn:  # this rank's rows against all rows
+                flops = 2.0 * (hi - lo) * w["n"] * w["d"]
             ach = flops / per_launch_s / 1e12
             peak = peaks["bf16_sustained"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
@@ -468,9 +511,11 @@ def main():
         base_np = shard.cpu().numpy()
         q_np = q.cpu().numpy()
         rate, m, t = cpu_sample_rate(w, base_np, q_np, args.cpu_budget)
+        what = (f"the lists of {m} rows (k + 1 search against all {w['n']} rows, then the "
+                f"row itself dropped)" if is_allnn else
+                f"{m} queries against all {w['n']} base rows")
         cpu = {"value": rate, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": f"{m} queries against all {w['n']} base rows ({t:.1f} s, OpenMP on "
-                         f"every host core)"}
+               "sample": f"{what} ({t:.1f} s, OpenMP on every host core)"}
 
     if rank == 0:
         value = w["nq"] * args.steps / (elapsed_ms / 1e3)
@@ -483,7 +528,9 @@ def main():
             "data": "synthetic (seeded, BASELINE distributions)",
             "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
                        "queries": w["nq"], "k": k,
-                       "parallelism": f"base rows sharded over {world} GPU(s)",
+                       "parallelism": (f"rows to list split over {world} GPU(s), all rows on "
+                                       f"each" if is_allnn else
+                                       f"base rows sharded over {world} GPU(s)"),
                        "l2_flush": "inputs larger than L2 (fp32 base 512 MB)"
                        if not is_hamming else "inputs larger than L2"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,

@@ -156,6 +156,44 @@ MLXVS_C_API int mlxvs_knn_keys_device(
     uint64_t* keys,
     void* stream);
 
+/**
+ * Exact k-nearest-neighbor graph of rows [n, d] (host, row-major float32):
+ * for every row, its k nearest OTHER rows, nearest first, ids [n, k] and
+ * distances [n, k] as mlxvs_brute_force_knn returns them (-1 / +-inf where
+ * fewer than k exist).  Requires 1 <= k <= 255, n >= 2 and d >= 1.
+ * Replaces: mlxvs::all_neighbors with algo BruteForce and one cluster
+ * (include/mlxvs/mlxvs.h:187-205, src/all_neighbors.cpp:250-263,364-377);
+ * the reference has no C entry for it.  The row itself is excluded inside
+ * the search instead of searching k + 1 and dropping it
+ * (src/all_neighbors.cpp:56-95).
+ */
+MLXVS_C_API int mlxvs_all_neighbors(
+    const float* rows,
+    int64_t n,
+    int32_t d,
+    int32_t k,
+    mlxvs_metric metric,
+    int32_t* ids,
+    float* distances);
+
+/**
+ * Device-pointer variant of mlxvs_all_neighbors for the rows
+ * query_begin .. query_end - 1 (their lists [query_end - query_begin, k]),
+ * so that devices holding all rows can split the graph by rows.
+ * Replaces: as mlxvs_all_neighbors.
+ */
+MLXVS_C_API int mlxvs_all_neighbors_device(
+    const float* rows,
+    int64_t n,
+    int32_t d,
+    int32_t k,
+    mlxvs_metric metric,
+    int64_t query_begin,
+    int64_t query_end,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
 /** Hamming shard: keys of score -distance (see mlxvs_knn_keys_device).
  * Replaces: the tile step of src/ivf.cpp:1370-1387 across devices. */
 MLXVS_C_API int mlxvs_hamming_keys_device(

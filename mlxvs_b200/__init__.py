@@ -27,7 +27,10 @@ import numpy as np
 
 __all__ = [
     "Metric",
+    "GraphBuild",
     "brute_force_knn",
+    "all_neighbors",
+    "all_neighbors_rows",
     "hamming_knn",
     "knn_keys",
     "hamming_keys",
@@ -72,6 +75,8 @@ def _load():
         "mlxvs_hamming_knn_device": [p, i64, p, i64, i32, i32, p, p, p],
         "mlxvs_knn_keys_device": [p, i64, p, i64, i32, i32, ctypes.c_int, i64, p, p],
         "mlxvs_hamming_keys_device": [p, i64, p, i64, i32, i32, i64, p, p],
+        "mlxvs_all_neighbors": [p, i64, i32, i32, ctypes.c_int, p, p],
+        "mlxvs_all_neighbors_device": [p, i64, i32, i32, ctypes.c_int, i64, i64, p, p, p],
         "mlxvs_merge_keys_device": [p, i32, i64, i32, i32, p, i32, p, p, p],
         "mlxvs_device_synchronize": [p],
         "mlxvs_profile_enable": [i32],
@@ -193,6 +198,98 @@ def brute_force_knn(base, queries, k, metric=Metric.l2, *, tile_rows=65536, stre
     _check(lib.mlxvs_brute_force_knn(
         b.ctypes.data, b.shape[0], q.ctypes.data, nq, b.shape[1], k, int(m),
         ids.ctypes.data, dist.ctypes.data))
+    return ids, dist
+
+
+class GraphBuild(enum.IntEnum):
+    """How all_neighbors builds each cluster's graph (include/mlxvs/mlxvs.h:
+    143-149)."""
+
+    brute_force = 0
+    nn_descent = 1
+
+
+def _graph_build(algo):
+    if isinstance(algo, str):
+        try:
+            return GraphBuild[algo]
+        except KeyError:
+            names = ", ".join(repr(n) for n in GraphBuild.__members__)
+            raise ValueError(f"unknown GraphBuild {algo!r}; one of {names}") from None
+    return GraphBuild(int(algo))
+
+
+def all_neighbors(rows, k, metric=Metric.l2, *, algo=GraphBuild.nn_descent, n_clusters=0,
+                  overlap_factor=2, brute_force_below=4096, max_cluster_rows=0, verbose=False,
+                  max_iterations=24, termination_threshold=1e-4, fp16=True, seed=42,
+                  stream=None):
+    """k-nearest-neighbor graph of the rows: every row's k nearest other rows,
+    nearest first, with the ids and distances of brute_force_knn (-1 and
+    +inf / -inf where fewer than k other rows exist).
+
+    Same arguments, checks and results as the reference's all_neighbors
+    (python/bindings.cpp:1183-1215, src/all_neighbors.cpp:265-300) on its
+    exact path: one cluster (n_clusters 0 or 1) built by brute force, which
+    the reference takes for algo brute_force and, with nn_descent, for
+    n <= max(brute_force_below, k + 1).  The clustered and NN-Descent builds
+    are not part of this library and raise NotImplementedError.  The
+    NN-Descent tuning arguments are accepted and unused.
+    """
+    op = "mlxvs::all_neighbors"
+    m = _metric(metric)
+    g = _graph_build(algo)
+    lib = _load()
+    k = int(k)
+    on_device = _is_torch(rows) and rows.is_cuda
+    if on_device:
+        x = _dev_float_rows(rows, op, "rows")
+    else:
+        x = _host_float_rows(rows, op, "rows")
+    n, d = int(x.shape[0]), int(x.shape[1])
+    max_k = 128 if g == GraphBuild.nn_descent else 255
+    if k < 1 or k > max_k or n < 2 or d < 1:
+        raise ValueError(f"[{op}] 1 <= k <= {max_k}, n >= 2 and d >= 1")
+    if n_clusters < 0 or n_clusters > n or overlap_factor < 1 or (
+            n_clusters > 1 and overlap_factor > n_clusters):
+        raise ValueError(
+            f"[{op}] 0 <= n_clusters <= n and 1 <= overlap_factor <= n_clusters")
+    exact = n_clusters <= 1 and (
+        g == GraphBuild.brute_force or n <= max(int(brute_force_below), k + 1))
+    if not exact:
+        raise NotImplementedError(
+            f"[{op}] only the exact one-cluster build is implemented (algo='brute_force' "
+            "with n_clusters 0 or 1, or n <= brute_force_below)")
+    if on_device:
+        torch = _torch()
+        ids = torch.empty((n, k), dtype=torch.int32, device=x.device)
+        dist = torch.empty((n, k), dtype=torch.float32, device=x.device)
+        with torch.cuda.device(x.device):
+            _check(lib.mlxvs_all_neighbors_device(
+                x.data_ptr(), n, d, k, int(m), 0, n, ids.data_ptr(), dist.data_ptr(),
+                _stream_handle(stream, x.device)))
+        return ids, dist
+    ids = np.empty((n, k), np.int32)
+    dist = np.empty((n, k), np.float32)
+    _check(lib.mlxvs_all_neighbors(x.ctypes.data, n, d, k, int(m), ids.ctypes.data,
+                                   dist.ctypes.data))
+    return ids, dist
+
+
+def all_neighbors_rows(rows, k, metric=Metric.l2, *, begin, end, stream=None):
+    """The exact all_neighbors lists of rows begin .. end - 1 only (CUDA
+    tensors): how devices that each hold all rows split the graph."""
+    op = "mlxvs::all_neighbors"
+    m = _metric(metric)
+    lib = _load()
+    torch = _torch()
+    x = _dev_float_rows(rows, op, "rows")
+    n, d = int(x.shape[0]), int(x.shape[1])
+    ids = torch.empty((max(0, end - begin), int(k)), dtype=torch.int32, device=x.device)
+    dist = torch.empty((max(0, end - begin), int(k)), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _check(lib.mlxvs_all_neighbors_device(
+            x.data_ptr(), n, d, int(k), int(m), int(begin), int(end), ids.data_ptr(),
+            dist.data_ptr(), _stream_handle(stream, x.device)))
     return ids, dist
 
 

@@ -132,6 +132,41 @@ int mlxvs_brute_force_knn(const float* base, int64_t n, const float* queries, in
   });
 }
 
+int mlxvs_all_neighbors(const float* rows, int64_t n, int32_t d, int32_t k, mlxvs_metric metric,
+                        int32_t* ids, float* distances) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(rows, n, d);
+    mlxvs_b200::Metric m = to_metric(metric);
+    require(k >= 1 && k <= 255 && n >= 2,
+            "[mlxvs::all_neighbors] 1 <= k <= 255, n >= 2 and d >= 1");
+    cudaStream_t s = thread_stream();
+    DeviceBuffers buf(s);
+    const size_t rbytes = (size_t)n * d * sizeof(float);
+    const size_t count = (size_t)n * k;
+    float* dr = static_cast<float*>(buf.alloc(rbytes));
+    int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
+    float* ddist = distances ? static_cast<float*>(buf.alloc(count * sizeof(float))) : nullptr;
+    ck(cudaMemcpyAsync(dr, rows, rbytes, cudaMemcpyHostToDevice, s), "copy rows");
+    mlxvs_b200::all_neighbors(dr, n, d, k, m, 0, n, dids, ddist, s);
+    ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
+    if (distances)
+      ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),
+         "copy distances");
+    mlxvs_b200::device_synchronize(s);
+  });
+}
+
+int mlxvs_all_neighbors_device(const float* rows, int64_t n, int32_t d, int32_t k,
+                               mlxvs_metric metric, int64_t query_begin, int64_t query_end,
+                               int32_t* ids, float* distances, void* stream) {
+  return guarded([&] {
+    host_rows(rows, n, d);
+    mlxvs_b200::all_neighbors(rows, n, d, k, to_metric(metric), query_begin, query_end, ids,
+                              distances, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int mlxvs_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
                       int32_t bytes, int32_t k, int32_t* ids, float* distances) {
   return guarded([&] {

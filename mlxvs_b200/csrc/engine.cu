@@ -276,7 +276,7 @@ void check_rows(int64_t n, const char* what) {
 //   4. merge of the units' lists into the k best, then distances.
 void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
               Metric metric, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
-              cudaStream_t s) {
+              cudaStream_t s, int64_t self_base = -1) {
   require(k >= 1 && k <= 256, "[mlxvs::brute_force_knn] k must be in [1, 256].");
   require(d >= 1, "[mlxvs::brute_force_knn] the dimension must be at least 1.");
   check_rows(n, "base rows");
@@ -353,22 +353,25 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   }
 
   // kernel shape, in order of preference: 128 queries per CTA with the
-  // 256 columns of a tile split over two warp groups (two heaps per query),
-  // then one warp group, then 64 .. 8 queries per CTA for large k (the MMA
-  // still computes 128 rows; the other lanes are unused); the query block
-  // resident in shared memory when it fits; the deepest ring that fits
+  // 256 columns of a tile split over two warp groups (two lists per query,
+  // in registers for k <= 32 even with a shallower ring, else heaps in
+  // shared memory), then one warp group, then 64 .. 8 queries per CTA for
+  // large k (the MMA still computes 128 rows; the other lanes are unused);
+  // the query block resident in shared memory when it fits; the deepest
+  // ring that fits
   const int npa = exact ? 1 : 2;
   const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
   int QB = 0, CG = 0, KR = 0, stages = 0, a_stream = 0;
   const int want_stages = exact ? 4 : 2;
-  // k <= 16 keeps each query's list in registers (two column groups)
-  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : 0));
+  // k <= 32 keeps each query's list in registers (two column groups)
+  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0)));
   struct Shape { int qb, cg, kr, min_st; };
-  const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, 0, want_stages},
+  const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, kr, 2},
+                         {128, 2, 0, want_stages},
                          {128, 1, 0, want_stages},  {64, 1, 0, want_stages},
                          {32, 1, 0, want_stages},   {16, 1, 0, want_stages},
-                         {8, 1, 0, want_stages},    {128, 2, kr, 2},
-                         {128, 2, 0, 2},            {128, 1, 0, 2},
+                         {8, 1, 0, want_stages},    {128, 2, 0, 2},
+                         {128, 1, 0, 2},
                          {64, 1, 0, 2},             {32, 1, 0, 2},
                          {16, 1, 0, 2},             {8, 1, 0, 2}};
   for (const Shape& sh : order) {
@@ -426,6 +429,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.gfloor = gfloor;
   p.done = done;
   p.out_scale = out_scale;
+  p.self_base = self_base;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
   const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k, fold, KR, nbm);
@@ -445,6 +449,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   MLXVS_GEMM(128, 2, 8)
   MLXVS_GEMM(128, 2, 12)
   MLXVS_GEMM(128, 2, 16)
+  MLXVS_GEMM(128, 2, 32)
   MLXVS_GEMM(128, 2, 0)
   MLXVS_GEMM(128, 1, 0)
   MLXVS_GEMM(64, 1, 0)
@@ -586,6 +591,21 @@ void knn_keys(const float* base, int64_t n, const float* queries, int64_t nq, in
               Metric metric, int64_t id_offset, uint64_t* keys, cudaStream_t s) {
   require(keys != nullptr || nq == 0, "[mlxvs::brute_force_knn] keys must not be NULL.");
   knn_core(base, n, queries, nq, d, k, metric, id_offset, keys, nullptr, nullptr, s);
+}
+
+void all_neighbors(const float* rows, int64_t n, int d, int k, Metric metric,
+                   int64_t query_begin, int64_t query_end, int32_t* ids, float* dist,
+                   cudaStream_t s) {
+  require(k >= 1 && k <= 255 && n >= 2 && d >= 1,
+          "[mlxvs::all_neighbors] 1 <= k <= 255, n >= 2 and d >= 1");
+  require(query_begin >= 0 && query_begin <= query_end && query_end <= n,
+          "[mlxvs::all_neighbors] 0 <= query_begin <= query_end <= n");
+  require(ids != nullptr || query_end == query_begin,
+          "[mlxvs::all_neighbors] ids must not be NULL.");
+  // every row is a query against all rows, its own row excluded in the
+  // kernel (the reference searches k + 1 and drops it in merge_lists)
+  knn_core(rows, n, rows + query_begin * d, query_end - query_begin, d, k, metric, 0, nullptr,
+           ids, dist, s, query_begin);
 }
 
 void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,

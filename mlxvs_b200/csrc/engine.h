@@ -32,6 +32,14 @@ void brute_force_knn(const float* base, int64_t n, const float* queries, int64_t
 void knn_keys(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
               Metric metric, int64_t id_offset, uint64_t* keys, cudaStream_t s);
 
+/** Exact k-NN graph of rows [n, d]: for rows query_begin .. query_end - 1,
+ * the k nearest other rows, as brute_force_knn returns them (ids, dist
+ * [query_end - query_begin, k]).  ref: all_neighbors with algo BruteForce
+ * and one cluster, src/all_neighbors.cpp:56-95,250-263,364-377. */
+void all_neighbors(const float* rows, int64_t n, int d, int k, Metric metric,
+                   int64_t query_begin, int64_t query_end, int32_t* ids, float* dist,
+                   cudaStream_t s);
+
 /** Exact Hamming k-NN.  ref: hamming_knn, src/ivf.cpp:1343-1403. */
 void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
                  int k, int32_t* ids, float* dist, cudaStream_t s);

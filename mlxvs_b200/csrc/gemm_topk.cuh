@@ -59,6 +59,9 @@ struct KnnGemmParams {
   unsigned long long* gfloor;      // [nq_pad] shared floor keys (0 = none)
   int* done;                       // [qblocks] 1 + the latest split whose lists are written
   float out_scale;                 // partial scores are written as score * out_scale
+  // >= 0: query q is the row with id self_base + q, which is never its own
+  // neighbor (all_neighbors); -1: none
+  int64_t self_base;
   uint32_t* err;                   // error word (bounded waits that gave up)
   uint64_t wait_ns;                // limit of every wait
 };
@@ -143,6 +146,7 @@ __device__ __forceinline__ void heap_replace_root(uint64_t* heap, int k, uint64_
 }
 
 struct EpiState {
+  uint32_t self_id;  // the query's own row id (all_neighbors), else 0xFFFFFFFF
   uint64_t floor;  // no candidate at or below this key can be in the result
   uint64_t gfl;    // the shared floor as last read or raised by this thread
   float thr;       // score of floor (-inf when none): the fast rejection test
@@ -163,7 +167,7 @@ __device__ __noinline__ EpiState epi_slow16(float v0, float v1, float v2, float 
     const float vj = v[j];
     if (vj >= st.thr && col0 + j < n_valid) {
       const uint64_t key = make_key(vj, id0 + (uint32_t)j);
-      if (key > st.floor) {
+      if (key > st.floor && id0 + (uint32_t)j != st.self_id) {
         heap_replace_root<HS>(heap, k, key);
         const uint64_t root = heap[0];
         if (root > st.floor) st.floor = root;
@@ -176,6 +180,15 @@ __device__ __noinline__ EpiState epi_slow16(float v0, float v1, float v2, float 
 
 // Waits on the register outputs of the preceding tcgen05.ld so the compiler
 // cannot read them before the load has completed.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
@@ -222,8 +235,8 @@ __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
 
 // 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
 // with one compare when their max is below the floor, else offer each.
-template <int HS, int NBM, int KR>
-__device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const float* nbs,
+template <int HS, int NBM, int KR, int RN>
+__device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const float* nbs,
                                           int64_t col0, const KnnGemmParams& p, bool row_on,
                                           uint64_t* heap, uint64_t (&key)[KR > 0 ? KR : 1],
                                           float* sv, EpiState& st) {
@@ -275,8 +288,9 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[32], int o, const 
           const int j = __ffs(mask) - 1;
           mask &= mask - 1;
           const float vj = sv[j * 32];
-          const uint64_t x = make_key(vj, id0 + (uint32_t)j);
-          if (x > st.floor) {
+          const uint32_t id = id0 + (uint32_t)j;
+          const uint64_t x = make_key(vj, id);
+          if (x > st.floor && id != st.self_id) {
             list_insert<KR>(key, x);
             if (key[0] > st.floor) st.floor = key[0];
             st.thr = key_score(st.floor);
@@ -577,6 +591,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
           for (int s = 0; s < p.k; ++s) heap[s * HS] = 0;
       }
       EpiState st;
+      st.self_id = (p.self_base >= 0 && q_ok) ? (uint32_t)(p.self_base + q) : 0xFFFFFFFFu;
       st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q) : 0ull;
       if (inherited > st.gfl) st.gfl = inherited;
       st.floor = st.gfl;
@@ -613,6 +628,31 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         const uint32_t taddr =
             tmem_base + ((uint32_t)(rg * 32) << 16) + acc * GT_BN + (uint32_t)(ch * CW);
         const int64_t col_base = (int64_t)t * GT_BN + ch * CW;
+        if constexpr (KR >= 32) {
+          // the long register lists leave room for 16-column loads only
+          uint32_t ra[16], rb[16];
+          tmem_ld16(taddr, ra);
+          tmem_wait_ld_regs(ra);
+#pragma unroll 1
+          for (int c = 0; c < 2 * NCH; c += 2) {
+            __syncwarp();
+            tmem_ld16(taddr + (c + 1) * 16, rb);
+            epi_sub16<HS, NBM, KR>(ra, 0, nbw + c * 16, col_base + c * 16, p, row_on, heap, key, sv, st);
+            __syncwarp();
+            tmem_wait_ld_regs(rb);
+            if (c + 2 < 2 * NCH) {
+              tmem_ld16(taddr + (c + 2) * 16, ra);
+            } else {
+              tc_fence_before();
+              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            epi_sub16<HS, NBM, KR>(rb, 0, nbw + c * 16 + 16, col_base + c * 16 + 16, p, row_on, heap, key, sv, st);
+            if (c + 2 < 2 * NCH) {
+              __syncwarp();
+              tmem_wait_ld_regs(ra);
+            }
+          }
+        } else {
         uint32_t ra[32], rb[32];
         tmem_ld32(taddr, ra);
         tmem_wait_ld_regs(ra);
@@ -637,6 +677,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             __syncwarp();
             tmem_wait_ld_regs(ra);
           }
+        }
         }
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;

@@ -137,3 +137,35 @@ def decode_keys(keys):
     ids[empty] = -1
     scores[empty] = -np.inf
     return ids, scores
+
+
+def all_neighbors(rows, k, metric="l2", threads=0, begin=0, end=None):
+    """Exact k-NN graph, as the reference builds it with algo BruteForce and
+    one cluster: brute_force_knn of the rows against themselves with
+    min(k + 1, n) neighbors (src/all_neighbors.cpp:250-263), then
+    merge_lists (:56-95): entries that are -1 or the row itself are dropped,
+    the rest ordered by distance (nearest first; ties keep the id order of
+    the argsort by id, i.e. lower id first), the best k kept, -1 / +-inf
+    padding.  begin / end: the lists of those rows only."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    n = rows.shape[0]
+    end = n if end is None else end
+    kk = min(k + 1, n)
+    ids, dist = brute_force_knn(rows, rows[begin:end], kk, metric, threads)
+    l2 = metric_code(metric) == L2
+    key = (dist if l2 else -dist).astype(np.float64)
+    dropped = (ids < 0) | (ids == np.arange(begin, end, dtype=np.int64)[:, None])
+    key[dropped] = np.inf
+    out_ids = np.full((end - begin, k), -1, np.int32)
+    out_dist = np.full((end - begin, k), np.inf if l2 else -np.inf, np.float32)
+    for i in range(end - begin):
+        by_id = np.argsort(ids[i], kind="stable")
+        sid, skey, sdist = ids[i][by_id], key[i][by_id], dist[i][by_id]
+        repeat = np.concatenate([[False], sid[1:] == sid[:-1]])
+        skey = np.where(repeat, np.inf, skey)
+        best = np.argsort(skey, kind="stable")[:k]
+        kept = skey[best] < np.inf
+        m = len(best)
+        out_ids[i, :m] = np.where(kept, sid[best], -1)
+        out_dist[i, :m] = np.where(kept, sdist[best], out_dist[i, :m])
+    return out_ids, out_dist

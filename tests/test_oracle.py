@@ -123,3 +123,32 @@ def test_invalid_arguments():
         O.brute_force_knn(b, b, 300, "l2")
     with pytest.raises(ValueError):
         O.brute_force_knn(b, b, 0, "l2")
+
+
+def test_all_neighbors_small_n_kats():
+    # python/tests/test_mlxvs.py:192-195: 5 rows, k = 8: the 4 other rows,
+    # then -1; tests/test_all_neighbors.cpp:76-98: 10 rows, k = 32: every
+    # other row once, then -1
+    ids, dist = O.all_neighbors(data.normal_rows(5, 4, 1), 8, "l2")
+    assert (ids[:, :4] >= 0).all() and (ids[:, 4:] == -1).all()
+    assert np.isinf(dist[:, 4:]).all()
+    ids, _ = O.all_neighbors(data.normal_rows(10, 7, 21), 32, "l2")
+    for i in range(10):
+        assert sorted(ids[i, :9].tolist()) == [j for j in range(10) if j != i]
+        assert (ids[i, 9:] == -1).all()
+
+
+@pytest.mark.parametrize("metric", ["l2", "inner_product"])
+def test_all_neighbors_is_self_excluded_topk(metric):
+    # the k + 1 search and merge_lists equal the top k of every other row
+    # (integer data: exact scores, ties to the lower id)
+    x, _ = data.gaussian_mixture_int(600, 16, 6, seed=5)
+    x = np.rint(x / 16.0).astype(np.float32)  # many ties
+    k = 12
+    ids, dist = O.all_neighbors(x, k, metric)
+    scores = data.exact_scores(metric, x, x)
+    np.fill_diagonal(scores, -np.inf)
+    order = np.lexsort((np.broadcast_to(np.arange(600), scores.shape), -scores), axis=1)[:, :k]
+    assert np.array_equal(ids, order)
+    want = np.take_along_axis(scores, order, 1)
+    assert np.array_equal(dist, (-want if metric == "l2" else want).astype(np.float32))
