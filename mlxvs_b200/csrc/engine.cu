@@ -367,13 +367,12 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0)));
   struct Shape { int qb, cg, kr, min_st; };
   const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, kr, 2},
-                         {128, 2, 0, want_stages},
-                         {128, 1, 0, want_stages},  {64, 1, 0, want_stages},
-                         {32, 1, 0, want_stages},   {16, 1, 0, want_stages},
-                         {8, 1, 0, want_stages},    {128, 2, 0, 2},
-                         {128, 1, 0, 2},
-                         {64, 1, 0, 2},             {32, 1, 0, 2},
-                         {16, 1, 0, 2},             {8, 1, 0, 2}};
+                         {128, 2, 0, want_stages},  {128, 2, 0, 2},
+                         {128, 1, 0, want_stages},  {128, 1, 0, 2},
+                         {64, 1, 0, want_stages},   {64, 1, 0, 2},
+                         {32, 1, 0, want_stages},   {32, 1, 0, 2},
+                         {16, 1, 0, want_stages},   {16, 1, 0, 2},
+                         {8, 1, 0, want_stages},    {8, 1, 0, 2}};
   for (const Shape& sh : order) {
     if (sh.cg == 2 && sh.kr == 0 && kr != 0) continue;  // the register list is the better form
     for (int as : {0, 1}) {
