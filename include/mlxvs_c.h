@@ -194,6 +194,83 @@ MLXVS_C_API int mlxvs_all_neighbors_device(
     float* distances,
     void* stream);
 
+/**
+ * One merge step of the exact search, for tests and benchmarks: the best k
+ * of each row of scores [nq, t] (host, row-major float32; ids id_offset +
+ * column) together with the running lists ids / best [nq, k], which are
+ * ignored (may be NULL) when first != 0.  Writes out_ids / out_scores
+ * [nq, k], best first (higher score, then lower id as unsigned), -1 / -inf
+ * where fewer than k exist.  1 <= k <= 256.
+ * Replaces: mlxvs::topk_merge (include/mlxvs/mlxvs.h:898-905,
+ * src/knn.cpp:37-69, kernel src/kernels.h:37-229); no C entry in the
+ * reference.
+ */
+MLXVS_C_API int mlxvs_topk_merge(
+    const float* scores,
+    int64_t nq,
+    int32_t t,
+    const int32_t* ids,
+    const float* best,
+    int32_t id_offset,
+    int32_t first,
+    int32_t k,
+    int32_t* out_ids,
+    float* out_scores);
+
+/** mlxvs_topk_merge on device pointers, enqueued on stream.
+ * Replaces: as mlxvs_topk_merge. */
+MLXVS_C_API int mlxvs_topk_merge_device(
+    const float* scores,
+    int64_t nq,
+    int32_t t,
+    const int32_t* ids,
+    const float* best,
+    int32_t id_offset,
+    int32_t first,
+    int32_t k,
+    int32_t* out_ids,
+    float* out_scores,
+    void* stream);
+
+/**
+ * Exact re-ranking: the k nearest of each query's candidate ids
+ * candidates [nq, c] (ids into dataset [n, d]; ids outside [0, n) are
+ * skipped) by exact distances, nearest first, as mlxvs_brute_force_knn
+ * returns them (-1 / +-inf where fewer than k are valid).  Equal distances
+ * keep the candidates' order.  Host buffers; only the distinct candidate
+ * rows are copied to the device.  1 <= k <= c.
+ * Replaces: mlxvs::refine (include/mlxvs/mlxvs.h:853-865,
+ * src/ivf.cpp:1642-1708); no C entry in the reference.
+ */
+MLXVS_C_API int mlxvs_refine(
+    const float* dataset,
+    int64_t n,
+    int32_t d,
+    const float* queries,
+    int64_t nq,
+    const int32_t* candidates,
+    int32_t c,
+    int32_t k,
+    mlxvs_metric metric,
+    int32_t* ids,
+    float* distances);
+
+/** mlxvs_refine on device pointers (the whole dataset on the device),
+ * enqueued on stream.  Replaces: as mlxvs_refine. */
+MLXVS_C_API int mlxvs_refine_device(
+    const float* dataset,
+    int64_t n,
+    int32_t d,
+    const float* queries,
+    int64_t nq,
+    const int32_t* candidates,
+    int32_t c,
+    int32_t k,
+    mlxvs_metric metric,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+
 /** Hamming shard: keys of score -distance (see mlxvs_knn_keys_device).
  * Replaces: the tile step of src/ivf.cpp:1370-1387 across devices. */
 MLXVS_C_API int mlxvs_hamming_keys_device(

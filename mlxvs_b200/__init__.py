@@ -31,6 +31,8 @@ __all__ = [
     "brute_force_knn",
     "all_neighbors",
     "all_neighbors_rows",
+    "topk_merge",
+    "refine",
     "hamming_knn",
     "knn_keys",
     "hamming_keys",
@@ -76,6 +78,10 @@ def _load():
         "mlxvs_knn_keys_device": [p, i64, p, i64, i32, i32, ctypes.c_int, i64, p, p],
         "mlxvs_hamming_keys_device": [p, i64, p, i64, i32, i32, i64, p, p],
         "mlxvs_all_neighbors": [p, i64, i32, i32, ctypes.c_int, p, p],
+        "mlxvs_topk_merge": [p, i64, i32, p, p, i32, i32, i32, p, p],
+        "mlxvs_topk_merge_device": [p, i64, i32, p, p, i32, i32, i32, p, p, p],
+        "mlxvs_refine": [p, i64, i32, p, i64, p, i32, i32, ctypes.c_int, p, p],
+        "mlxvs_refine_device": [p, i64, i32, p, i64, p, i32, i32, ctypes.c_int, p, p, p],
         "mlxvs_all_neighbors_device": [p, i64, i32, i32, ctypes.c_int, i64, i64, p, p, p],
         "mlxvs_merge_keys_device": [p, i32, i64, i32, i32, p, i32, p, p, p],
         "mlxvs_device_synchronize": [p],
@@ -290,6 +296,122 @@ def all_neighbors_rows(rows, k, metric=Metric.l2, *, begin, end, stream=None):
         _check(lib.mlxvs_all_neighbors_device(
             x.data_ptr(), n, d, int(k), int(m), int(begin), int(end), ids.data_ptr(),
             dist.data_ptr(), _stream_handle(stream, x.device)))
+    return ids, dist
+
+
+def topk_merge(scores, ids, best, id_offset, first, k, *, stream=None):
+    """One merge step of the exact search: the best k of each row of scores
+    [nq, t] (ids id_offset + column) together with the running lists ids
+    (int32) and best (float32) [nq, k], which are ignored when first is set.
+    Returns (ids int32 [nq, k], scores float32 [nq, k]), best first (higher
+    score, then lower id as unsigned), -1 / -inf padded.
+
+    Same arguments, checks and results as the reference's topk_merge
+    (include/mlxvs/mlxvs.h:898-905, src/knn.cpp:37-69).  NumPy in, NumPy
+    out; CUDA tensors in, CUDA tensors out.
+    """
+    op = "mlxvs::topk_merge"
+    lib = _load()
+    k = int(k)
+    first = bool(first)
+    if _is_torch(scores) and scores.is_cuda:
+        torch = _torch()
+        if scores.dim() != 2 or scores.dtype != torch.float32:
+            raise ValueError(f"[{op}] scores must be float32 [nq, t]")
+        sc = scores.contiguous()
+        nq, t = int(sc.shape[0]), int(sc.shape[1])
+        if not first:
+            pi = ids.to(device=sc.device, dtype=torch.int32).contiguous()
+            pb = best.to(device=sc.device, dtype=torch.float32).contiguous()
+            if tuple(pi.shape) != (nq, k) or tuple(pb.shape) != (nq, k):
+                raise ValueError(f"[{op}] ids and best must be [nq, k]")
+        out_ids = torch.empty((nq, max(k, 0)), dtype=torch.int32, device=sc.device)
+        out_sc = torch.empty((nq, max(k, 0)), dtype=torch.float32, device=sc.device)
+        with torch.cuda.device(sc.device):
+            _check(lib.mlxvs_topk_merge_device(
+                sc.data_ptr(), nq, t, None if first else pi.data_ptr(),
+                None if first else pb.data_ptr(), int(id_offset), int(first), k,
+                out_ids.data_ptr(), out_sc.data_ptr(), _stream_handle(stream, sc.device)))
+        return out_ids, out_sc
+    sc = scores.detach().cpu().numpy() if _is_torch(scores) else np.asarray(scores)
+    if sc.ndim != 2 or sc.dtype != np.float32:
+        raise ValueError(f"[{op}] scores must be float32 [nq, t]")
+    sc = np.ascontiguousarray(sc)
+    nq, t = sc.shape
+    pi = pb = None
+    if not first:
+        pi = np.ascontiguousarray(np.asarray(ids), dtype=np.int32)
+        pb = np.ascontiguousarray(np.asarray(best), dtype=np.float32)
+        if pi.shape != (nq, k) or pb.shape != (nq, k):
+            raise ValueError(f"[{op}] ids and best must be [nq, k]")
+    out_ids = np.empty((nq, max(k, 0)), np.int32)
+    out_sc = np.empty((nq, max(k, 0)), np.float32)
+    _check(lib.mlxvs_topk_merge(
+        sc.ctypes.data, nq, t, None if first else pi.ctypes.data,
+        None if first else pb.ctypes.data, int(id_offset), int(first), k,
+        out_ids.ctypes.data, out_sc.ctypes.data))
+    return out_ids, out_sc
+
+
+def refine(dataset, queries, candidates, k, metric="l2", *, stream=None):
+    """Exact re-ranking, as cuVS's refine: the k nearest of each query's
+    candidate ids [nq, c] (ids outside [0, n) skipped) by exact distances,
+    nearest first; (ids int32 [nq, k], distances float32 [nq, k]) as
+    brute_force_knn returns them.  Equal distances keep the candidates'
+    order; repeated candidates are all kept, as in the reference.
+
+    Same arguments and results as the reference's refine
+    (python/mlxvs/_ivf.py:158-185, src/ivf.cpp:1642-1708).  With NumPy
+    inputs only the distinct candidate rows are copied to the device; with
+    CUDA tensors everything stays on the device.
+    """
+    op = "mlxvs::refine"
+    m = _metric(metric)
+    lib = _load()
+    k = int(k)
+    if _is_torch(dataset) and dataset.is_cuda:
+        torch = _torch()
+        ds = _dev_float_rows(dataset, op, "dataset")
+        q = queries if _is_torch(queries) else torch.as_tensor(np.asarray(queries))
+        q = q.to(ds.device)
+        if q.dim() == 1:
+            q = q[None]
+        q = _dev_float_rows(q, op, "queries")
+        cand = candidates if _is_torch(candidates) else torch.as_tensor(np.asarray(candidates))
+        cand = cand.to(device=ds.device, dtype=torch.int64)
+        cand = torch.where((cand >= 0) & (cand < ds.shape[0]), cand, -1)
+        cand = cand.to(torch.int32).contiguous()
+        nq, d = int(q.shape[0]), int(q.shape[1])
+        if ds.shape[1] != d or cand.dim() != 2 or cand.shape[0] != nq:
+            raise ValueError(f"[{op}] dataset [n, d], queries [nq, d] and candidates [nq, c] "
+                             "must match.")
+        c = int(cand.shape[1])
+        ids = torch.empty((nq, max(k, 0)), dtype=torch.int32, device=ds.device)
+        dist = torch.empty((nq, max(k, 0)), dtype=torch.float32, device=ds.device)
+        with torch.cuda.device(ds.device):
+            _check(lib.mlxvs_refine_device(
+                ds.data_ptr(), int(ds.shape[0]), d, q.data_ptr(), nq, cand.data_ptr(), c, k,
+                int(m), ids.data_ptr(), dist.data_ptr(), _stream_handle(stream, ds.device)))
+        return ids, dist
+    ds = _host_float_rows(dataset, op, "dataset")
+    q = np.asarray(queries.detach().cpu() if _is_torch(queries) else queries)
+    if q.ndim == 1:
+        q = q[None]
+    q = _host_float_rows(q, op, "queries")
+    cand = np.asarray(candidates.detach().cpu() if _is_torch(candidates) else candidates)
+    nq, d = q.shape
+    if ds.shape[1] != d or cand.ndim != 2 or cand.shape[0] != nq:
+        raise ValueError(f"[{op}] dataset [n, d], queries [nq, d] and candidates [nq, c] "
+                         "must match.")
+    cand64 = cand.astype(np.int64)
+    # ids outside the dataset (also those beyond int32) are skipped as -1
+    cand32 = np.where((cand64 >= 0) & (cand64 < ds.shape[0]), cand64, -1).astype(np.int32)
+    cand32 = np.ascontiguousarray(cand32)
+    c = cand32.shape[1]
+    ids = np.empty((nq, max(k, 0)), np.int32)
+    dist = np.empty((nq, max(k, 0)), np.float32)
+    _check(lib.mlxvs_refine(ds.ctypes.data, ds.shape[0], d, q.ctypes.data, nq, cand32.ctypes.data,
+                            c, k, int(m), ids.ctypes.data, dist.ctypes.data))
     return ids, dist
 
 

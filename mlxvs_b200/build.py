@@ -14,7 +14,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmlxvs_b200.so")
 SOURCES = ["engine.cu", "c_api.cpp"]
-HEADERS = ["common.cuh", "gemm_topk.cuh", "hamming.cuh", "knn_kernels.cuh", "engine.h"]
+HEADERS = ["common.cuh", "gemm_topk.cuh", "hamming.cuh", "knn_kernels.cuh", "select.cuh",
+           "engine.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

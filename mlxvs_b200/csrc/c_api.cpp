@@ -4,9 +4,11 @@
 // cleared on success (ref: src/c_api.cpp:28-47).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "engine.h"
 #include "mlxvs_c.h"
@@ -164,6 +166,113 @@ int mlxvs_all_neighbors_device(const float* rows, int64_t n, int32_t d, int32_t 
     host_rows(rows, n, d);
     mlxvs_b200::all_neighbors(rows, n, d, k, to_metric(metric), query_begin, query_end, ids,
                               distances, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_topk_merge_device(const float* scores, int64_t nq, int32_t t, const int32_t* ids,
+                            const float* best, int32_t id_offset, int32_t first, int32_t k,
+                            int32_t* out_ids, float* out_scores, void* stream) {
+  return guarded([&] {
+    mlxvs_b200::topk_merge(scores, nq, t, ids, best, id_offset, first != 0, k, out_ids,
+                           out_scores, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_topk_merge(const float* scores, int64_t nq, int32_t t, const int32_t* ids,
+                     const float* best, int32_t id_offset, int32_t first, int32_t k,
+                     int32_t* out_ids, float* out_scores) {
+  return guarded([&] {
+    require(k >= 1 && k <= 256, "[mlxvs::topk_merge] k must be in [1, 256]");
+    require(nq >= 0 && t >= 0, "[mlxvs::topk_merge] scores must be float32 [nq, t]");
+    require(out_ids != nullptr && out_scores != nullptr,
+            "[mlxvs::topk_merge] outputs must not be NULL.");
+    require(first || (ids != nullptr && best != nullptr),
+            "[mlxvs::topk_merge] ids and best [nq, k] are needed unless first.");
+    if (nq == 0) return;
+    cudaStream_t s = thread_stream();
+    DeviceBuffers buf(s);
+    const size_t sbytes = (size_t)nq * t * sizeof(float);
+    const size_t count = (size_t)nq * k;
+    float* ds = static_cast<float*>(buf.alloc(sbytes));
+    int32_t* dprev = first ? nullptr : static_cast<int32_t*>(buf.alloc(count * 4));
+    float* dbest = first ? nullptr : static_cast<float*>(buf.alloc(count * 4));
+    int32_t* dids = static_cast<int32_t*>(buf.alloc(count * 4));
+    float* dout = static_cast<float*>(buf.alloc(count * 4));
+    if (sbytes) ck(cudaMemcpyAsync(ds, scores, sbytes, cudaMemcpyHostToDevice, s), "copy scores");
+    if (!first) {
+      ck(cudaMemcpyAsync(dprev, ids, count * 4, cudaMemcpyHostToDevice, s), "copy ids");
+      ck(cudaMemcpyAsync(dbest, best, count * 4, cudaMemcpyHostToDevice, s), "copy best");
+    }
+    mlxvs_b200::topk_merge(ds, nq, t, dprev, dbest, id_offset, first != 0, k, dids, dout, s);
+    ck(cudaMemcpyAsync(out_ids, dids, count * 4, cudaMemcpyDeviceToHost, s), "copy ids");
+    ck(cudaMemcpyAsync(out_scores, dout, count * 4, cudaMemcpyDeviceToHost, s), "copy scores");
+    mlxvs_b200::device_synchronize(s);
+  });
+}
+
+int mlxvs_refine_device(const float* dataset, int64_t n, int32_t d, const float* queries,
+                        int64_t nq, const int32_t* candidates, int32_t c, int32_t k,
+                        mlxvs_metric metric, int32_t* ids, float* distances, void* stream) {
+  return guarded([&] {
+    mlxvs_b200::refine(dataset, n, d, queries, nq, candidates, c, k, to_metric(metric), ids,
+                       distances, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_refine(const float* dataset, int64_t n, int32_t d, const float* queries, int64_t nq,
+                 const int32_t* candidates, int32_t c, int32_t k, mlxvs_metric metric,
+                 int32_t* ids, float* distances) {
+  return guarded([&] {
+    require(ids != nullptr, "ids must not be NULL.");
+    host_rows(dataset, n, d);
+    host_rows(queries, nq, d);
+    mlxvs_b200::Metric m = to_metric(metric);
+    require(c >= 0 && k >= 1 && k <= c,
+            "[mlxvs::refine] k must be in [1, candidates per query].");
+    if (nq == 0) return;
+    require(candidates != nullptr, "candidates must not be NULL.");
+    // only the distinct candidate rows travel to the device (the dataset
+    // may be far larger than the candidates), with the candidates renumbered
+    std::vector<int32_t> uniq;
+    uniq.reserve((size_t)nq * c);
+    for (int64_t i = 0; i < nq * (int64_t)c; ++i)
+      if (candidates[i] >= 0 && candidates[i] < n) uniq.push_back(candidates[i]);
+    std::sort(uniq.begin(), uniq.end());
+    uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+    std::vector<int32_t> local((size_t)nq * c);
+    for (int64_t i = 0; i < nq * (int64_t)c; ++i) {
+      const int32_t id = candidates[i];
+      local[i] = (id >= 0 && id < n)
+                     ? (int32_t)(std::lower_bound(uniq.begin(), uniq.end(), id) - uniq.begin())
+                     : -1;
+    }
+    std::vector<float> rows(uniq.size() * (size_t)d);
+    for (size_t r = 0; r < uniq.size(); ++r)
+      std::memcpy(rows.data() + r * d, dataset + (size_t)uniq[r] * d, (size_t)d * sizeof(float));
+    cudaStream_t s = thread_stream();
+    DeviceBuffers buf(s);
+    const size_t count = (size_t)nq * k;
+    float* drows = static_cast<float*>(buf.alloc(rows.size() * sizeof(float)));
+    float* dq = static_cast<float*>(buf.alloc((size_t)nq * d * sizeof(float)));
+    int32_t* dc = static_cast<int32_t*>(buf.alloc(local.size() * sizeof(int32_t)));
+    int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
+    float* ddist = static_cast<float*>(buf.alloc(count * sizeof(float)));
+    if (!rows.empty())
+      ck(cudaMemcpyAsync(drows, rows.data(), rows.size() * sizeof(float), cudaMemcpyHostToDevice,
+                         s), "copy rows");
+    ck(cudaMemcpyAsync(dq, queries, (size_t)nq * d * sizeof(float), cudaMemcpyHostToDevice, s),
+       "copy queries");
+    ck(cudaMemcpyAsync(dc, local.data(), local.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                       s), "copy candidates");
+    mlxvs_b200::refine(drows, (int64_t)uniq.size(), d, dq, nq, dc, c, k, m, dids, ddist, s);
+    ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s),
+       "copy ids");
+    if (distances)
+      ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),
+         "copy distances");
+    mlxvs_b200::device_synchronize(s);
+    for (size_t i = 0; i < count; ++i)
+      if (ids[i] >= 0) ids[i] = uniq[(size_t)ids[i]];
   });
 }
 

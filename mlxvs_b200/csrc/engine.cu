@@ -12,6 +12,7 @@
 #include "engine.h"
 #include "gemm_topk.cuh"
 #include "hamming.cuh"
+#include "select.cuh"
 #include "knn_kernels.cuh"
 
 #ifndef MLXVS_B200_VERSION
@@ -605,6 +606,68 @@ void all_neighbors(const float* rows, int64_t n, int d, int k, Metric metric,
   // kernel (the reference searches k + 1 and drops it in merge_lists)
   knn_core(rows, n, rows + query_begin * d, query_end - query_begin, d, k, metric, 0, nullptr,
            ids, dist, s, query_begin);
+}
+
+void topk_merge(const float* scores, int64_t nq, int t, const int32_t* ids, const float* best,
+                int id_offset, bool first, int k, int32_t* out_ids, float* out_scores,
+                cudaStream_t s) {
+  require(k >= 1 && k <= TOPK_KMAX, "[mlxvs::topk_merge] k must be in [1, 256]");
+  require(nq >= 0 && t >= 0, "[mlxvs::topk_merge] scores must be float32 [nq, t]");
+  if (nq == 0) return;
+  require(scores != nullptr || t == 0, "[mlxvs::topk_merge] scores must not be NULL.");
+  require(first || (ids != nullptr && best != nullptr),
+          "[mlxvs::topk_merge] ids and best [nq, k] are needed unless first.");
+  require(out_ids != nullptr && out_scores != nullptr,
+          "[mlxvs::topk_merge] outputs must not be NULL.");
+  require(nq < (1LL << 31), "[mlxvs::topk_merge] at most 2^31 - 1 rows.");
+  device_info();
+  TopkRowsParams p{scores, nq, t, first ? nullptr : ids, first ? nullptr : best,
+                   id_offset, k, out_ids, out_scores};
+  ProfScope prof("topk_rows", s);
+  topk_rows_kernel<<<(unsigned)nq, TOPK_THREADS, 0, s>>>(p);
+  CK(cudaGetLastError());
+}
+
+void refine(const float* dataset, int64_t n, int d, const float* queries, int64_t nq,
+            const int32_t* candidates, int c, int k, Metric metric, int32_t* ids, float* dist,
+            cudaStream_t s) {
+  require(d >= 1 && n >= 0 && nq >= 0 && c >= 0,
+          "[mlxvs::refine] dataset [n, d], queries [nq, d] and candidates [nq, c] must match.");
+  require(k >= 1 && k <= c, "[mlxvs::refine] k must be in [1, candidates per query].");
+  require(k <= TOPK_KMAX, "[mlxvs::refine] k must be at most 256.");
+  const int mi = static_cast<int>(metric);
+  require(mi >= 0 && mi <= 2, "[mlxvs::refine] unknown metric.");
+  require(nq < (1LL << 31), "[mlxvs::refine] at most 2^31 - 1 queries.");
+  if (nq == 0) return;
+  require(queries != nullptr && candidates != nullptr && ids != nullptr,
+          "[mlxvs::refine] null input.");
+  require(dataset != nullptr || n == 0, "[mlxvs::refine] null dataset.");
+  device_info();
+  Scratch sc(s);
+  float* sc_scores = sc.alloc<float>((size_t)nq * c);
+  float* sel_scores = dist ? dist : sc.alloc<float>((size_t)nq * k);
+  RefineParams rp{dataset, n, d, queries, nq, candidates, c, mi, sc_scores};
+  {
+    const int64_t pairs = nq * (int64_t)c;
+    const int warps_per_block = 8;
+    require(pairs / warps_per_block < (1LL << 31), "[mlxvs::refine] too many candidates.");
+    ProfScope prof("refine_scores", s);
+    refine_scores_kernel<<<(unsigned)((pairs + warps_per_block - 1) / warps_per_block),
+                           warps_per_block * 32, 0, s>>>(rp);
+    CK(cudaGetLastError());
+  }
+  // positions 0 .. c-1 as ids: equal scores keep the candidates' order
+  TopkRowsParams tp{sc_scores, nq, c, nullptr, nullptr, 0, k, ids, sel_scores};
+  {
+    ProfScope prof("topk_rows", s);
+    topk_rows_kernel<<<(unsigned)nq, TOPK_THREADS, 0, s>>>(tp);
+    CK(cudaGetLastError());
+  }
+  const int64_t count = nq * (int64_t)k;
+  ProfScope prof("refine_finish", s);
+  refine_finish_kernel<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(
+      candidates, c, count, k, metric == Metric::L2 ? 1 : 0, ids, sel_scores);
+  CK(cudaGetLastError());
 }
 
 void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,

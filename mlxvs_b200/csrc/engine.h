@@ -40,6 +40,21 @@ void all_neighbors(const float* rows, int64_t n, int d, int k, Metric metric,
                    int64_t query_begin, int64_t query_end, int32_t* ids, float* dist,
                    cudaStream_t s);
 
+/** One merge step: the best k of each row of scores [nq, t] (ids
+ * id_offset + column) together with the running lists ids / best [nq, k]
+ * (ignored when first), best first: out_ids, out_scores [nq, k].
+ * ref: topk_merge, src/knn.cpp:37-69, include/mlxvs/mlxvs.h:898-905. */
+void topk_merge(const float* scores, int64_t nq, int t, const int32_t* ids, const float* best,
+                int id_offset, bool first, int k, int32_t* out_ids, float* out_scores,
+                cudaStream_t s);
+
+/** Exact re-ranking: the k nearest of each query's candidate ids [nq, c]
+ * (ids outside [0, n) skipped) by exact distances, nearest first, as
+ * brute_force_knn returns them.  ref: refine, src/ivf.cpp:1642-1708. */
+void refine(const float* dataset, int64_t n, int d, const float* queries, int64_t nq,
+            const int32_t* candidates, int c, int k, Metric metric, int32_t* ids, float* dist,
+            cudaStream_t s);
+
 /** Exact Hamming k-NN.  ref: hamming_knn, src/ivf.cpp:1343-1403. */
 void hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
                  int k, int32_t* ids, float* dist, cudaStream_t s);

@@ -1,0 +1,259 @@
+// Row-wise selection: the standalone topk_merge (one merge step of the
+// reference's tile loop, src/knn.cpp:37-69 with its kernel src/kernels.h:
+// 37-229) and the exact re-ranking refine (src/ivf.cpp:1642-1708), which
+// scores each query's candidates and selects with the same kernel.
+#pragma once
+
+#include "common.cuh"
+
+namespace mlxvs_b200 {
+
+constexpr int TOPK_THREADS = 256;  // threads per row (the reference's TOPK_THREADS)
+constexpr int TOPK_KMAX = 256;     // the largest k (TOPK_MAX)
+
+struct TopkRowsParams {
+  const float* scores;       // [nq][t] (row stride t)
+  int64_t nq;
+  int32_t t;
+  const int32_t* prev_ids;   // [nq][k] running list, or null (first)
+  const float* prev_scores;  // [nq][k]
+  int32_t id_offset;         // column j has id id_offset + j
+  int32_t k;
+  int32_t* out_ids;          // [nq][k]
+  float* out_scores;         // [nq][k]
+};
+
+// "a comes before b": higher score first, then lower id as unsigned (so -1
+// goes last); src/kernels.h:21-23.
+__device__ __forceinline__ bool topk_before(float sa, int32_t ia, float sb, int32_t ib) {
+  return sa > sb || (sa == sb && (uint32_t)ia < (uint32_t)ib);
+}
+
+// One block per row.  Candidates are the row's t scores and, unless first,
+// the k running entries; each is the 64-bit key (order bits of the score,
+// ~id), larger = better, so one radix select over the keys (8-bit digits
+// from the top, stopping as soon as the selected bucket is taken whole)
+// finds the k-th largest key and how many entries equal to it to keep.  One
+// pass gathers the winners; a bitonic sort orders them by topk_before.
+__global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams p) {
+  constexpr int WARPS = TOPK_THREADS / 32;
+  __shared__ uint32_t hist[WARPS][256];
+  __shared__ uint32_t suffix[256];
+  __shared__ unsigned long long s_prefix;
+  __shared__ uint32_t s_need, s_done;
+  __shared__ uint32_t taken_above, taken_equal;
+  __shared__ float sel_score[TOPK_KMAX];
+  __shared__ int32_t sel_id[TOPK_KMAX];
+
+  const int lid = threadIdx.x;
+  const int warp = lid >> 5;
+  const int64_t q = blockIdx.x;
+  if (q >= p.nq) return;
+  const uint32_t t = (uint32_t)p.t;
+  const uint32_t k = (uint32_t)p.k;
+  const bool has_prev = p.prev_ids != nullptr;
+  const uint32_t total = t + (has_prev ? k : 0u);
+  const uint32_t keff = k < total ? k : total;
+  const float* row = p.scores + q * (int64_t)t;
+  const int64_t prev = q * (int64_t)k;
+
+  auto candidate = [&](uint32_t i, float& v, int32_t& id) {
+    if (i < t) {
+      v = row[i];
+      id = p.id_offset + (int32_t)i;
+    } else {
+      v = p.prev_scores[prev + (i - t)];
+      id = p.prev_ids[prev + (i - t)];
+    }
+  };
+  auto key_of = [](float v, int32_t id) -> uint64_t {
+    return ((uint64_t)order_bits(v) << 32) | (uint64_t)(~(uint32_t)id);
+  };
+
+  uint64_t prefix = 0, mask = 0;
+  uint32_t need = keff;
+  if (keff > 0) {
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int i = lid; i < WARPS * 256; i += TOPK_THREADS) (&hist[0][0])[i] = 0u;
+      __syncthreads();
+      for (uint32_t i = lid; i < total; i += TOPK_THREADS) {
+        float v;
+        int32_t id;
+        candidate(i, v, id);
+        const uint64_t key = key_of(v, id);
+        if ((key & mask) == prefix) atomicAdd(&hist[warp][(uint32_t)(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      // per digit (one per thread) its count, then the counts of every digit
+      // at or above it; the selected digit is where that first reaches need
+      uint32_t c = 0;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) c += hist[w][lid];
+      suffix[lid] = c;
+      __syncthreads();
+      for (int off = 1; off < 256; off <<= 1) {
+        const uint32_t add = lid + off < 256 ? suffix[lid + off] : 0u;
+        __syncthreads();
+        suffix[lid] += add;
+        __syncthreads();
+      }
+      const uint32_t at_or_above = suffix[lid];
+      const uint32_t above = at_or_above - c;
+      if (at_or_above >= need && above < need) {
+        s_prefix = prefix | ((uint64_t)lid << shift);
+        s_need = need - above;
+        s_done = (c == need - above) ? 1u : 0u;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      need = s_need;
+      mask |= 255ull << shift;
+      const bool done = s_done != 0;
+      __syncthreads();
+      if (done) break;
+    }
+  }
+
+  // gather: every key above the k-th, and `need` of those equal to it (equal
+  // keys are equal entries, so which of them is immaterial)
+  if (lid == 0) {
+    taken_above = 0;
+    taken_equal = 0;
+  }
+  for (int i = lid; i < TOPK_KMAX; i += TOPK_THREADS) {
+    sel_score[i] = -INFINITY;
+    sel_id[i] = -1;
+  }
+  __syncthreads();
+  const uint32_t n_above = keff - need;
+  if (keff > 0) {
+    for (uint32_t i = lid; i < total; i += TOPK_THREADS) {
+      float v;
+      int32_t id;
+      candidate(i, v, id);
+      const uint64_t key = key_of(v, id) & mask;
+      if (key > prefix) {
+        const uint32_t at = atomicAdd(&taken_above, 1u);
+        sel_score[at] = v;
+        sel_id[at] = id;
+      } else if (key == prefix) {
+        const uint32_t at = atomicAdd(&taken_equal, 1u);
+        if (at < need) {
+          sel_score[n_above + at] = v;
+          sel_id[n_above + at] = id;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // bitonic sort of the winners, best first (src/kernels.h:196-222)
+  uint32_t size_pow2 = 1;
+  while (size_pow2 < keff) size_pow2 <<= 1;
+  for (uint32_t size = 2; size <= size_pow2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = lid; i < size_pow2; i += TOPK_THREADS) {
+        const uint32_t j = i ^ stride;
+        if (j > i) {
+          const bool forward = (i & size) == 0;
+          const float si = sel_score[i], sj = sel_score[j];
+          const int32_t ii = sel_id[i], ij = sel_id[j];
+          const bool in_order = topk_before(si, ii, sj, ij);
+          if (forward != in_order) {
+            sel_score[i] = sj;
+            sel_score[j] = si;
+            sel_id[i] = ij;
+            sel_id[j] = ii;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t i = lid; i < k; i += TOPK_THREADS) {
+    const bool ok = i < keff;
+    p.out_scores[prev + i] = ok ? sel_score[i] : -INFINITY;
+    p.out_ids[prev + i] = ok ? sel_id[i] : -1;
+  }
+}
+
+struct RefineParams {
+  const float* dataset;       // [n][d]
+  int64_t n;
+  int32_t d;
+  const float* queries;       // [nq][d]
+  int64_t nq;
+  const int32_t* candidates;  // [nq][c]
+  int32_t c;
+  int32_t metric;             // 0 inner product, 1 L2, 2 cosine
+  float* scores;              // [nq][c]: larger is closer, -inf where invalid
+};
+
+// One warp per (query, candidate): the exact score of the candidate row as
+// the reference computes it (src/ivf.cpp:1677-1690): L2 -sum((r - q)^2),
+// inner product sum(r q), cosine on rows and query divided by
+// max(norm, 1e-30).  Ids outside [0, n) score -inf.
+__global__ void refine_scores_kernel(RefineParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= p.nq * (int64_t)p.c) return;
+  const int64_t q = pair / p.c;
+  const int32_t id = p.candidates[pair];
+  if (id < 0 || (int64_t)id >= p.n) {
+    if (lane == 0) p.scores[pair] = -INFINITY;
+    return;
+  }
+  const float* r = p.dataset + (int64_t)id * p.d;
+  const float* x = p.queries + q * p.d;
+  float acc = 0.0f, rr = 0.0f, xx = 0.0f;
+  for (int j = lane; j < p.d; j += 32) {
+    const float a = __ldg(r + j);
+    const float b = __ldg(x + j);
+    if (p.metric == 1) {
+      const float df = a - b;
+      acc = fmaf(df, df, acc);
+    } else {
+      acc = fmaf(a, b, acc);
+      if (p.metric == 2) {
+        rr = fmaf(a, a, rr);
+        xx = fmaf(b, b, xx);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (p.metric == 2) {
+      rr += __shfl_xor_sync(0xffffffffu, rr, off);
+      xx += __shfl_xor_sync(0xffffffffu, xx, off);
+    }
+  }
+  if (lane == 0) {
+    float s;
+    if (p.metric == 1) {
+      s = -acc;
+    } else if (p.metric == 2) {
+      s = acc / (fmaxf(sqrtf(rr), 1e-30f) * fmaxf(sqrtf(xx), 1e-30f));
+    } else {
+      s = acc;
+    }
+    p.scores[pair] = s;
+  }
+}
+
+// Selected positions -> candidate ids and distances; infinite scores are
+// missing (-1, +inf for L2, -inf otherwise), as src/ivf.cpp:1694-1699.
+__global__ void refine_finish_kernel(const int32_t* __restrict__ candidates, int32_t c,
+                                     int64_t count, int32_t k, int32_t l2,
+                                     int32_t* __restrict__ ids, float* __restrict__ dist) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const int64_t q = i / k;
+  const int32_t pos = ids[i];
+  const float s = dist[i];
+  const bool missing = pos < 0 || isinf(s);
+  ids[i] = missing ? -1 : candidates[q * c + pos];
+  dist[i] = l2 ? (missing ? INFINITY : -s) : (missing ? -INFINITY : s);
+}
+
+}  // namespace mlxvs_b200

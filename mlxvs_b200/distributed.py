@@ -18,9 +18,11 @@ path.
 import torch
 import torch.distributed as dist
 
-from . import KIND_HAMMING, Metric, _metric, hamming_keys, knn_keys, merge_keys
+from . import (KIND_HAMMING, Metric, _metric, all_neighbors_rows, hamming_keys, knn_keys,
+               merge_keys)
 
-__all__ = ["shard_bounds", "gather_lists", "sharded_brute_force_knn", "sharded_hamming_knn"]
+__all__ = ["shard_bounds", "gather_lists", "sharded_brute_force_knn", "sharded_hamming_knn",
+           "sharded_all_neighbors"]
 
 
 def shard_bounds(n, world):
@@ -62,6 +64,37 @@ def sharded_hamming_knn(rows_shard, queries, k, *, id_offset, group=None, stream
     keys = hamming_keys(rows_shard, queries, k, id_offset=id_offset, stream=stream)
     lists = gather_lists(keys, group)
     return merge_keys(lists, k, "hamming", stream=stream)
+
+
+def sharded_all_neighbors(rows, k, metric=Metric.l2, *, group=None, stream=None, gather=True):
+    """Exact k-NN graph of rows (a CUDA tensor, the same on every rank): each
+    rank lists its contiguous share of the rows against all rows, with no
+    exchange.  Returns (ids, distances) of the whole graph on every rank
+    (gather: an all-gather of the lists), else this rank's [hi - lo, k]
+    share and its (lo, hi)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    n = rows.shape[0]
+    b = shard_bounds(n, world)
+    lo, hi = b[rank], b[rank + 1]
+    ids, dst = all_neighbors_rows(rows, k, metric, begin=lo, end=hi, stream=stream)
+    if not gather:
+        return ids, dst, (lo, hi)
+    if world == 1:
+        return ids, dst
+    # equal-sized pieces for the all-gather: pad to the largest share
+    rows_max = max(b[r + 1] - b[r] for r in range(world))
+    pad = rows_max - (hi - lo)
+    if pad:
+        ids = torch.cat([ids, ids.new_full((pad, k), -1)])
+        dst = torch.cat([dst, dst.new_zeros((pad, k))])
+    all_ids = torch.empty((world * rows_max, k), dtype=ids.dtype, device=ids.device)
+    all_dst = torch.empty((world * rows_max, k), dtype=dst.dtype, device=dst.device)
+    dist.all_gather_into_tensor(all_ids, ids.contiguous(), group=group)
+    dist.all_gather_into_tensor(all_dst, dst.contiguous(), group=group)
+    keep = torch.cat([torch.arange(r * rows_max, r * rows_max + b[r + 1] - b[r],
+                                   device=ids.device) for r in range(world)])
+    return all_ids[keep], all_dst[keep]
 
 
 KIND = {"hamming": KIND_HAMMING}

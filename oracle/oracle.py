@@ -169,3 +169,67 @@ def all_neighbors(rows, k, metric="l2", threads=0, begin=0, end=None):
         out_ids[i, :m] = np.where(kept, sid[best], -1)
         out_dist[i, :m] = np.where(kept, sdist[best], out_dist[i, :m])
     return out_ids, out_dist
+
+
+def _order_bits(v):
+    """The sign-flip map of src/kernels.h:16-19 (float32 -> uint32, order kept)."""
+    u = np.ascontiguousarray(v, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+
+
+def topk_merge(scores, ids, best, id_offset, first, k):
+    """One merge step (src/knn.cpp:37-69, kernel src/kernels.h:37-229): per
+    row, the k largest (score key, then lower id as unsigned) of the t new
+    entries (ids id_offset + column) and, unless first, the k running ones;
+    then ordered by score (float compare) and id; -1 / -inf padding."""
+    scores = np.asarray(scores, dtype=np.float32)
+    nq, t = scores.shape
+    out_ids = np.full((nq, k), -1, np.int32)
+    out_sc = np.full((nq, k), -np.inf, np.float32)
+    for i in range(nq):
+        v = scores[i]
+        idv = (id_offset + np.arange(t, dtype=np.int64)).astype(np.int32)
+        if not first:
+            v = np.concatenate([v, np.asarray(best[i], np.float32)])
+            idv = np.concatenate([idv, np.asarray(ids[i], np.int32)])
+        key = (_order_bits(v) << np.uint64(32)) | (~idv.view(np.uint32)).astype(np.uint64)
+        take = np.argsort(key, kind="stable")[::-1][:k]
+        sv, si = v[take], idv[take]
+        order = np.lexsort((si.view(np.uint32), -sv.astype(np.float64)))
+        m = len(take)
+        out_ids[i, :m] = si[order]
+        out_sc[i, :m] = sv[order]
+    return out_ids, out_sc
+
+
+def refine(dataset, queries, candidates, k, metric="l2"):
+    """Exact re-ranking (src/ivf.cpp:1642-1708): float32 scores of each
+    candidate row (L2 -sum((r - q)^2), inner product, cosine on unit rows),
+    -inf for ids outside [0, n); the k best by a stable sort on -score
+    (equal scores keep the candidates' order); infinite scores are missing
+    (-1, +inf for L2, -inf otherwise)."""
+    ds = np.asarray(dataset, dtype=np.float32)
+    q = np.asarray(queries, dtype=np.float32)
+    cand = np.asarray(candidates).astype(np.int64)
+    n = ds.shape[0]
+    valid = (cand >= 0) & (cand < n)
+    rows = ds[np.where(valid, cand, 0)]
+    code = metric_code(metric)
+    qq = q[:, None, :]
+    if code == COSINE:
+        rows = rows / np.maximum(np.sqrt((rows * rows).sum(2, keepdims=True)), np.float32(1e-30))
+        qq = qq / np.maximum(np.sqrt((qq * qq).sum(2, keepdims=True)), np.float32(1e-30))
+    if code == L2:
+        score = -((rows - qq) ** 2).sum(2, dtype=np.float32)
+    else:
+        score = (rows * qq).sum(2, dtype=np.float32)
+    score = np.where(valid, score, -np.inf).astype(np.float32)
+    order = np.argsort(-score, axis=1, kind="stable")[:, :k]
+    best = np.take_along_axis(score, order, 1)
+    missing = np.isinf(best)
+    ids = np.where(missing, -1, np.take_along_axis(cand, order, 1)).astype(np.int32)
+    if code == L2:
+        dist = np.where(missing, np.inf, -best)
+    else:
+        dist = np.where(missing, -np.inf, best)
+    return ids, dist.astype(np.float32)

@@ -70,6 +70,13 @@ def _worker(rank, world, port, out):
                     scores = data.exact_scores(metric, q, b)
                     single = data.recall(ids.cpu().numpy(), scores, k, tol=1e-4) == 1.0
             out[(rank, metric, k, integer)] = (same, single)
+        # the k-NN graph split by rows (all rows on every rank, no exchange
+        # but the final gather)
+        x, _ = data.gaussian_mixture_int(20_001, 64, 16, seed=44)
+        tx = torch.from_numpy(x).to(dev)
+        gids, gdist = mvd.sharded_all_neighbors(tx, 16, "l2")
+        sids, sdist = mv.all_neighbors(tx, 16, "l2", algo="brute_force")
+        out[(rank, "allnn")] = bool(torch.equal(gids, sids) and torch.equal(gdist, sdist))
     finally:
         dist.destroy_process_group()
 
@@ -90,3 +97,5 @@ def test_two_gpus_match_single():
             assert same, (r, metric, k, integer)
             if r == 0:
                 assert single, (metric, k, integer)
+    for r in range(WORLD):
+        assert res[(r, "allnn")], r

@@ -152,3 +152,35 @@ def test_all_neighbors_is_self_excluded_topk(metric):
     assert np.array_equal(ids, order)
     want = np.take_along_axis(scores, order, 1)
     assert np.array_equal(dist, (-want if metric == "l2" else want).astype(np.float32))
+
+
+def test_topk_merge_oracle_order():
+    # the running list and the new scores merged: best score first, equal
+    # scores by id as unsigned (-1 last), src/kernels.h:21-23
+    rng = np.random.default_rng(7)
+    s = rng.integers(0, 4, (5, 40)).astype(np.float32)
+    ids0, sc0 = O.topk_merge(s, None, None, 50, True, 12)
+    ids1, sc1 = O.topk_merge(s, ids0, sc0, 7, False, 12)
+    for i in range(5):
+        cand = [(float(v), 50 + j) for j, v in enumerate(s[i])] + \
+               [(float(v), 7 + j) for j, v in enumerate(s[i])]
+        cand.sort(key=lambda e: (-e[0], e[1] & 0xFFFFFFFF))
+        assert ids1[i].tolist() == [e[1] for e in cand[:12]]
+        assert sc1[i].tolist() == [e[0] for e in cand[:12]]
+    # fewer entries than k: -1 / -inf padding
+    ids, sc = O.topk_merge(s[:, :3], None, None, 0, True, 5)
+    assert (ids[:, 3:] == -1).all() and np.isneginf(sc[:, 3:]).all()
+
+
+def test_refine_oracle_matches_exact():
+    x, _ = data.gaussian_mixture_int(300, 16, 4, seed=9)
+    q = x[:20]
+    rng = np.random.default_rng(3)
+    cand = rng.integers(-5, 320, (20, 30))
+    ids, dist = O.refine(x, q, cand, 8, "l2")
+    for i in range(20):
+        rows = [(int(((x[c] - q[i]) ** 2).sum()), j, c) for j, c in enumerate(cand[i])
+                if 0 <= c < 300]
+        rows.sort(key=lambda e: (e[0], e[1]))
+        want = [c for _, _, c in rows[:8]] + [-1] * max(0, 8 - len(rows))
+        assert ids[i].tolist() == want
