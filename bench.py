@@ -400,6 +400,9 @@ def main():
     elapsed_ms = t0.elapsed_time(t1)
     kname = "hamming_topk" if is_hamming else "gemm_topk"
     kern_ms, kern_launches = mv.profile_read(kname)
+    if is_hamming and kern_launches == 0:  # the tensor-core path ran
+        kname = "hamming_mma"
+        kern_ms, kern_launches = mv.profile_read(kname)
     _, all_launches = mv.profile_read(None)
     mv.profile_enable(False)
     clocks = sampler.stop() if sampler else None
@@ -482,7 +485,22 @@ def main():
     if kern_launches > 0:
         per_launch_s = kern_ms / kern_launches / 1e3
         n_local = hi - lo
-        if is_hamming:
+        if is_hamming and kname == "hamming_mma":
+            # codes as +-1 int8 on the tensor cores: 2 * Q * N * bits integer
+            # ops per launch, against twice the measured bf16 rate (int8 runs
+            # at twice the bf16 rate on this part; no int8 peak is measured)
+            bits = w["bytes"] * 8
+            ops = 2.0 * w["nq"] * n_local * bits
+            ach = ops / per_launch_s / 1e12
+            peak = 2.0 * peaks["bf16_sustained"]
+            roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
+                    "frac": ach / peak, "traffic": None,
+                    "peak_source": f"2 x {peaks['source']} bf16 sustained",
+                    "kernel": kname, "kernel_ms": per_launch_s * 1e3,
+                    "algorithmic_per_launch": f"2*Q*N*bits = {ops:.3e} int8 ops "
+                                              f"({w['nq'] * n_local * (bits // 32):.3e} "
+                                              f"32-bit popcounts' worth)"}
+        elif is_hamming:
             # integer work: 32-bit popcounts per launch; reported against the
             # HBM copy bandwidth is meaningless here (compute bound), so the
             # unit is the popcount rate
@@ -524,7 +542,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": "u8" if is_hamming else "f16",
+            "dtype": ("s8" if kname == "hamming_mma" else "u8") if is_hamming else "f16",
             "data": "synthetic (seeded, BASELINE distributions)",
             "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
                        "queries": w["nq"], "k": k,

@@ -190,6 +190,18 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// The same with signed 8-bit operands and signed 32-bit accumulators
+// (kind::i8; K = 32 bytes per instruction, the same smem stepping as f16).
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on bar when every tcgen05.mma issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -265,6 +277,16 @@ __device__ __forceinline__ uint64_t sdesc_k32(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4)                       // D format: f32
          | (0u << 7) | (0u << 10)        // A, B format: f16
+         | (0u << 15) | (0u << 16)       // A, B K-major
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor of kind::i8: signed 8-bit A and B (K-major), s32
+// accumulators, M x N.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N) {
+  return (2u << 4)                       // D format: s32
+         | (1u << 7) | (1u << 10)        // A, B format: signed 8-bit
          | (0u << 15) | (0u << 16)       // A, B K-major
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16

@@ -251,12 +251,12 @@ struct GemmMaps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo, b_x;
 };
 
-template <int QB, int NPASS, int CG, int NBM, int KR>
+template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0>
 void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t smem,
                  cudaStream_t s) {
-  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR>;
+  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ProfScope prof("gemm_topk", s);
+  ProfScope prof(OP == 1 ? "hamming_mma" : "gemm_topk", s);
   kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo,
                                                               m.b_x, p);
   CK(cudaGetLastError());
@@ -266,6 +266,41 @@ void check_rows(int64_t n, const char* what) {
   require(n >= 0 && n < (1LL << 31),
           std::string("[mlxvs::brute_force_knn] the number of ") + what +
               " must be in [0, 2^31).");
+}
+
+struct GemmShape {
+  int qb, cg, kr, stages, a_stream;
+};
+
+// The fused kernel's shape, in order of preference: 128 queries per CTA
+// with the 256 columns of a tile split over two warp groups (two lists per
+// query, in registers for k <= 32 even with a shallower ring, else heaps in
+// shared memory), then one warp group, then 64 .. 8 queries per CTA for
+// large k (the MMA still computes 128 rows; the other lanes are unused);
+// the query block resident in shared memory when it fits; the deepest ring
+// that fits.
+GemmShape choose_shape(const DeviceInfo& dev, int npa, int kchunks, int k, int extra, int nbm,
+                       int want_stages) {
+  const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
+  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0)));
+  struct Shape { int qb, cg, kr, min_st; };
+  const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, kr, 2},
+                         {128, 2, 0, want_stages},  {128, 2, 0, 2},
+                         {128, 1, 0, want_stages},  {128, 1, 0, 2},
+                         {64, 1, 0, want_stages},   {64, 1, 0, 2},
+                         {32, 1, 0, want_stages},   {32, 1, 0, 2},
+                         {16, 1, 0, want_stages},   {16, 1, 0, 2},
+                         {8, 1, 0, want_stages},    {8, 1, 0, 2}};
+  for (const Shape& sh : order) {
+    if (sh.cg == 2 && sh.kr == 0 && kr != 0) continue;  // the register list is the better form
+    for (int as : {0, 1}) {
+      for (int st = 8; st >= sh.min_st; --st) {
+        if (gemm_smem(sh.qb, npa, sh.cg, kchunks, st, as, k, extra, sh.kr, nbm).total <= budget)
+          return GemmShape{sh.qb, sh.cg, sh.kr, st, as};
+      }
+    }
+  }
+  throw std::runtime_error("[mlxvs_b200] no kernel shape fits shared memory");
 }
 
 // The exact k-NN of queries among base: keys [nq, k] (out_keys) and / or ids
@@ -353,45 +388,10 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
     out_scale = std::ldexp(1.0f, -(eb + eq));
   }
 
-  // kernel shape, in order of preference: 128 queries per CTA with the
-  // 256 columns of a tile split over two warp groups (two lists per query,
-  // in registers for k <= 32 even with a shallower ring, else heaps in
-  // shared memory), then one warp group, then 64 .. 8 queries per CTA for
-  // large k (the MMA still computes 128 rows; the other lanes are unused);
-  // the query block resident in shared memory when it fits; the deepest
-  // ring that fits
   const int npa = exact ? 1 : 2;
-  const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
-  int QB = 0, CG = 0, KR = 0, stages = 0, a_stream = 0;
-  const int want_stages = exact ? 4 : 2;
-  // k <= 32 keeps each query's list in registers (two column groups)
-  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0)));
-  struct Shape { int qb, cg, kr, min_st; };
-  const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, kr, 2},
-                         {128, 2, 0, want_stages},  {128, 2, 0, 2},
-                         {128, 1, 0, want_stages},  {128, 1, 0, 2},
-                         {64, 1, 0, want_stages},   {64, 1, 0, 2},
-                         {32, 1, 0, want_stages},   {32, 1, 0, 2},
-                         {16, 1, 0, want_stages},   {16, 1, 0, 2},
-                         {8, 1, 0, want_stages},    {8, 1, 0, 2}};
-  for (const Shape& sh : order) {
-    if (sh.cg == 2 && sh.kr == 0 && kr != 0) continue;  // the register list is the better form
-    for (int as : {0, 1}) {
-      for (int st = 8; st >= sh.min_st; --st) {
-        if (gemm_smem(sh.qb, npa, sh.cg, kchunks, st, as, k, fold, sh.kr, nbm).total <= budget) {
-          QB = sh.qb;
-          CG = sh.cg;
-          KR = sh.kr;
-          stages = st;
-          a_stream = as;
-          break;
-        }
-      }
-      if (QB) break;
-    }
-    if (QB) break;
-  }
-  if (QB == 0) throw std::runtime_error("[mlxvs_b200] no kernel shape fits shared memory");
+  const GemmShape shape = choose_shape(dev, npa, kchunks, k, fold ? 1 : 0, nbm, exact ? 4 : 2);
+  const int QB = shape.qb, CG = shape.cg, KR = shape.kr, stages = shape.stages,
+            a_stream = shape.a_stream;
   const int qblocks = (int)((nq + QB - 1) / QB);
   const int tiles = (int)(n_pad / GT_BN);
   const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
@@ -508,6 +508,99 @@ void launch_hamming_v(const HammingParams& p, int QH, const DeviceInfo& dev, Scr
   return launch_hamming_t<V, 64>(p, dev, sc, out, s);
 }
 
+// Hamming k-NN on the tensor cores: codes unpacked to +-1 int8 rows, one
+// kind::i8 MMA pass of the fused kernel (s32 dots, exact), scores
+// -(bits - dot) / 2 = -distance, so the keys equal those of the popcount
+// kernel.  Returns false (nothing enqueued) when the unpacked rows would
+// take more than half of the free device memory.
+bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
+                 int k, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
+                 cudaStream_t s) {
+  DeviceInfo& dev = device_info();
+  const int bits = bytes * 8;
+  const int d_pad = (int)round_up(bits, 128);  // one 128-byte K chunk per 128 bits
+  const int kchunks = d_pad / 128;
+  const int64_t n_pad = round_up(n, GT_BN);
+  const int64_t nq_pad = round_up(nq, 128);
+  size_t free_b = 0, total_b = 0;
+  CK(cudaMemGetInfo(&free_b, &total_b));
+  if ((double)(n_pad + nq_pad) * d_pad > 0.5 * (double)free_b) return false;
+  const GemmShape sh = choose_shape(dev, 1, kchunks, k, 0, 1, 4);
+  Scratch sc(s);
+  int8_t* b8 = sc.alloc<int8_t>((size_t)n_pad * d_pad);
+  int8_t* q8 = sc.alloc<int8_t>((size_t)nq_pad * d_pad);
+  {
+    ProfScope prof("prep", s);
+    const int64_t gb = std::min<int64_t>((n_pad * (d_pad / 16) + 255) / 256, (int64_t)dev.sms * 32);
+    hamming_unpack_kernel<<<(unsigned)gb, 256, 0, s>>>(rows, n, n_pad, bytes, d_pad, b8);
+    CK(cudaGetLastError());
+    const int64_t gq = std::min<int64_t>((nq_pad * (d_pad / 16) + 255) / 256, (int64_t)dev.sms * 32);
+    hamming_unpack_kernel<<<(unsigned)gq, 256, 0, s>>>(queries, nq, nq_pad, bytes, d_pad, q8);
+    CK(cudaGetLastError());
+  }
+  const int qblocks = (int)((nq + sh.qb - 1) / sh.qb);
+  const int tiles = (int)(n_pad / GT_BN);
+  const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
+  uint64_t* partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
+  unsigned long long* gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
+  CK(cudaMemsetAsync(gfloor, 0, (size_t)nq_pad * 8, s));
+  int* done = sc.alloc<int>((size_t)qblocks);
+  CK(cudaMemsetAsync(done, 0, (size_t)qblocks * 4, s));
+  // int8 rows through the fp16 tensor maps: d_pad bytes = d_pad / 2 halves
+  GemmMaps maps;
+  maps.a_hi = map_f16(reinterpret_cast<__half*>(q8), d_pad / 2, nq_pad, GT_KCH, sh.qb);
+  maps.b_hi = map_f16(reinterpret_cast<__half*>(b8), d_pad / 2, n_pad, GT_KCH, GT_BN);
+  maps.a_lo = maps.a_hi;
+  maps.b_lo = maps.b_hi;
+  maps.b_x = maps.b_hi;
+  KnnGemmParams p{};
+  p.qblocks = qblocks;
+  p.tiles = tiles;
+  p.splits = splits;
+  p.units = qblocks * splits;
+  p.kchunks = kchunks;
+  p.k = k;
+  p.stages = sh.stages;
+  p.a_stream = sh.a_stream;
+  p.extra = 0;
+  p.n_valid = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.id_offset = id_offset;
+  p.nb = nullptr;
+  p.partial = partial;
+  p.gfloor = gfloor;
+  p.done = done;
+  p.out_scale = 1.0f;
+  p.dot_offset = -0.5f * (float)bits;
+  p.self_base = -1;
+  p.err = dev.err;
+  p.wait_ns = WAIT_LIMIT_NS;
+  const GemmSmem lay = gemm_smem(sh.qb, 1, sh.cg, kchunks, sh.stages, sh.a_stream, k, 0, sh.kr, 1);
+  const uint32_t smem = lay.total + 1024u;
+  const int grid = std::min(p.units, dev.sms);
+  bool launched = false;
+#define MLXVS_HGEMM(QB_, CG_, KR_)                                      \
+  if (!launched && sh.qb == QB_ && sh.cg == CG_ && sh.kr == KR_) {     \
+    launch_gemm<QB_, 1, CG_, 1, KR_, 1>(maps, p, grid, smem, s);       \
+    launched = true;                                                   \
+  }
+  MLXVS_HGEMM(128, 2, 8)
+  MLXVS_HGEMM(128, 2, 12)
+  MLXVS_HGEMM(128, 2, 16)
+  MLXVS_HGEMM(128, 2, 32)
+  MLXVS_HGEMM(128, 2, 0)
+  MLXVS_HGEMM(128, 1, 0)
+  MLXVS_HGEMM(64, 1, 0)
+  MLXVS_HGEMM(32, 1, 0)
+  MLXVS_HGEMM(16, 1, 0)
+  MLXVS_HGEMM(8, 1, 0)
+#undef MLXVS_HGEMM
+  require(launched, "[mlxvs_b200] hamming: no tensor-core kernel for this shape");
+  launch_merge(partial, splits, nq_pad, nq, k, KIND_HAMMING, nullptr, out_keys, ids, dist, s);
+  return true;
+}
+
 void hamming_core(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
                   int k, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
                   cudaStream_t s) {
@@ -527,6 +620,7 @@ void hamming_core(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_
     return;
   }
   require(rows != nullptr && queries != nullptr, "[mlxvs::hamming_knn] null input.");
+  if (hamming_mma(rows, n, queries, nq, bytes, k, id_offset, out_keys, ids, dist, s)) return;
   int V = 1;
   while (V * 16 < bytes) V <<= 1;
   const int row_bytes = 16 * V;

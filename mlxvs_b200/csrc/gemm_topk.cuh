@@ -59,6 +59,9 @@ struct KnnGemmParams {
   unsigned long long* gfloor;      // [nq_pad] shared floor keys (0 = none)
   int* done;                       // [qblocks] 1 + the latest split whose lists are written
   float out_scale;                 // partial scores are written as score * out_scale
+  // OP 1 (Hamming on +-1 int8 codes): score = dot / 2 + dot_offset, with
+  // dot_offset = -bits / 2, i.e. minus the Hamming distance
+  float dot_offset;
   // >= 0: query q is the row with id self_base + q, which is never its own
   // neighbor (all_neighbors); -1: none
   int64_t self_base;
@@ -235,14 +238,19 @@ __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
 
 // 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
 // with one compare when their max is below the floor, else offer each.
-template <int HS, int NBM, int KR, int RN>
+template <int HS, int NBM, int KR, int OP, int RN>
 __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const float* nbs,
                                           int64_t col0, const KnnGemmParams& p, bool row_on,
                                           uint64_t* heap, uint64_t (&key)[KR > 0 ? KR : 1],
                                           float* sv, EpiState& st) {
   float v[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[o + j]);
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (OP == 1)  // s32 dot of +-1 codes -> -(Hamming distance), exact
+      v[j] = fmaf(__int2float_rn((int32_t)r[o + j]), 0.5f, p.dot_offset);
+    else
+      v[j] = __uint_as_float(r[o + j]);
+  }
   if (NBM == 0) {
     const float4* nb4 = reinterpret_cast<const float4*>(nbs);
 #pragma unroll
@@ -302,7 +310,7 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const 
   }
 }
 
-template <int QB, int NPASS, int CG, int NBM, int KR>
+template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0>
 __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     knn_gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                          const __grid_constant__ CUtensorMap tm_a_lo,
@@ -314,7 +322,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
   constexpr int HS = CG * QB;     // heap slot stride
   constexpr int CW = GT_BN / CG;  // columns per epilogue warp per tile
   constexpr int NCH = CW / 32;    // chunks of 32 columns (even)
-  constexpr uint32_t IDESC = idesc_f16_f32(128, GT_BN);
+  constexpr uint32_t IDESC = OP == 1 ? idesc_i8_s32(128, GT_BN) : idesc_f16_f32(128, GT_BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
@@ -508,8 +516,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < GT_KCH / 16; ++kk) {
               const uint32_t acc_in = (kc | kk) != 0 || p.extra;
-              umma_f16_ss(d_tmem, sdesc_k128(a_hi + kk * 32), sdesc_k128(b_hi + kk * 32), IDESC,
-                          acc_in);
+              if constexpr (OP == 1)
+                umma_i8_ss(d_tmem, sdesc_k128(a_hi + kk * 32), sdesc_k128(b_hi + kk * 32), IDESC,
+                           acc_in);
+              else
+                umma_f16_ss(d_tmem, sdesc_k128(a_hi + kk * 32), sdesc_k128(b_hi + kk * 32),
+                            IDESC, acc_in);
               if (NPASS == 3) {
                 umma_f16_ss(d_tmem, sdesc_k128(a_hi + kk * 32), sdesc_k128(b_lo + kk * 32),
                             IDESC, 1u);
@@ -637,7 +649,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
           for (int c = 0; c < 2 * NCH; c += 2) {
             __syncwarp();
             tmem_ld16(taddr + (c + 1) * 16, rb);
-            epi_sub16<HS, NBM, KR>(ra, 0, nbw + c * 16, col_base + c * 16, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP>(ra, 0, nbw + c * 16, col_base + c * 16, p, row_on, heap, key, sv, st);
             __syncwarp();
             tmem_wait_ld_regs(rb);
             if (c + 2 < 2 * NCH) {
@@ -646,7 +658,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
               tc_fence_before();
               if (lane == 0) mbar_arrive(&acc_empty[acc]);
             }
-            epi_sub16<HS, NBM, KR>(rb, 0, nbw + c * 16 + 16, col_base + c * 16 + 16, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP>(rb, 0, nbw + c * 16 + 16, col_base + c * 16 + 16, p, row_on, heap, key, sv, st);
             if (c + 2 < 2 * NCH) {
               __syncwarp();
               tmem_wait_ld_regs(ra);
@@ -660,8 +672,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          epi_sub16<HS, NBM, KR>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
           __syncwarp();
           tmem_wait_ld_regs(rb);
           if (c + 2 < NCH) {
@@ -671,8 +683,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
-          epi_sub16<HS, NBM, KR>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
           if (c + 2 < NCH) {
             __syncwarp();
             tmem_wait_ld_regs(ra);

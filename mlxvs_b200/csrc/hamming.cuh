@@ -232,6 +232,38 @@ __global__ void __launch_bounds__(QH + 32)
   __syncthreads();
 }
 
+// Bit-packed codes [rows][bytes] -> +-1 int8 rows [rows_pad][d_pad] for the
+// tensor-core path: bit j of byte b is dimension 8 b + j, a 1 bit is +1 and
+// a 0 bit -1, and dimensions past the code and padding rows are 0.  The dot
+// of two such rows is then bits - 2 * (their Hamming distance), exactly.
+// One thread per two source bytes (16 output bytes).
+__global__ void hamming_unpack_kernel(const uint8_t* __restrict__ src, int64_t rows,
+                                      int64_t rows_pad, int32_t bytes, int32_t d_pad,
+                                      int8_t* __restrict__ dst) {
+  const int32_t pairs = d_pad / 16;
+  const int64_t total = rows_pad * pairs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / pairs;
+    const int32_t b0 = (int32_t)(i - r * pairs) * 2;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (r < rows) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (b0 + h < bytes) {
+          const uint32_t byte = src[r * bytes + b0 + h];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t v = ((byte >> j) & 1u) ? 0x01u : 0xFFu;
+            w[h * 2 + (j >> 2)] |= v << (8 * (j & 3));
+          }
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(dst + r * d_pad + (int64_t)b0 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 #endif  // __CUDACC__
 
 }  // namespace mlxvs_b200
