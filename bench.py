@@ -52,6 +52,11 @@ WORKLOADS = {
                             clusters=1024,
                             desc="config 3: all_neighbors of 1M x 128 fp32 (integer-valued "
                                  "mixture), L2, k=32 self excluded"),
+    # config 4's codes at a tenth of the rows: the profiling case (its
+    # unpacked rows, 1 GB, keep an ncu capture small)
+    "hamming-1m-1024b": dict(kind="hamming", n=1_000_000, nq=10_000, bytes=128, k=10,
+                             prototypes=4096, flip=0.1,
+                             desc="config 4 at 1M x 1024-bit codes, 10k queries, k=10"),
     # BASELINE config 4
     "hamming-10m-1024b": dict(kind="hamming", n=10_000_000, nq=10_000, bytes=128, k=10,
                               prototypes=4096, flip=0.1,
@@ -63,8 +68,12 @@ METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pi
 # DRAM bytes per launch of the dominant kernel, from the committed ncu
 # summaries under profiles/ (None until captured for that workload).
 NCU_TRAFFIC_PER_LAUNCH = {
-    # profiles/knn_gemm_topk_config1.md: 366.6 MB read + 14.1 MB written
-    "knn-l2-1m-k10": 380.7e6,
+    # profiles/knn_gemm_topk_config1.md: 386.8 MB read + 12.3 MB written
+    "knn-l2-1m-k10": 399.1e6,
+    # profiles/knn_gemm_topk_i8_hamming_1m.md: 3.32 GB at 1M codes
+    "hamming-1m-1024b": 3.322e9,
+    # the same, scaled by rows to 10M codes (10x the base tiles)
+    "hamming-10m-1024b": 33.22e9,
 }
 
 
@@ -494,7 +503,7 @@ def main():
             ach = ops / per_launch_s / 1e12
             peak = 2.0 * peaks["bf16_sustained"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
-                    "frac": ach / peak, "traffic": None,
+                    "frac": ach / peak, "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
                     "peak_source": f"2 x {peaks['source']} bf16 sustained",
                     "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"2*Q*N*bits = {ops:.3e} int8 ops "
