@@ -412,6 +412,13 @@ def main():
     if is_hamming and kern_launches == 0:  # the tensor-core path ran
         kname = "hamming_mma"
         kern_ms, kern_launches = mv.profile_read(kname)
+    coll_ms, coll_launches = mv.profile_read("gemm_collect")
+    if coll_launches > 0:
+        # k > 32: a sampled pass (lists of 1/4 of the base) and a collecting
+        # pass over the whole base make up one search; both are counted
+        kname = "gemm_topk (sampled pass) + gemm_collect"
+        kern_ms += coll_ms
+        kern_launches = coll_launches
     _, all_launches = mv.profile_read(None)
     mv.profile_enable(False)
     clocks = sampler.stop() if sampler else None

@@ -251,12 +251,12 @@ struct GemmMaps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo, b_x;
 };
 
-template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0>
+template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0, int MODE = 0>
 void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t smem,
                  cudaStream_t s) {
-  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP>;
+  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP, MODE>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ProfScope prof(OP == 1 ? "hamming_mma" : "gemm_topk", s);
+  ProfScope prof(OP == 1 ? "hamming_mma" : (MODE == 1 ? "gemm_collect" : "gemm_topk"), s);
   kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo,
                                                               m.b_x, p);
   CK(cudaGetLastError());
@@ -301,6 +301,141 @@ GemmShape choose_shape(const DeviceInfo& dev, int npa, int kchunks, int k, int e
     }
   }
   throw std::runtime_error("[mlxvs_b200] no kernel shape fits shared memory");
+}
+
+// Launches the fused kernel of shape (qb, cg, kr) and operand passes for the
+// given params (list mode, or collect mode for mode 1 with kr 8).
+void launch_shape(const GemmMaps& maps, const KnnGemmParams& p, int qb, int cg, int kr,
+                  bool exact, int nbm, int mode, uint32_t smem, int grid, cudaStream_t s) {
+  bool launched = false;
+#define MLXVS_GEMM_M(QB_, CG_, KR_, MODE_)                                   \
+  if (!launched && qb == QB_ && cg == CG_ && kr == KR_ && mode == MODE_) {   \
+    if (exact && nbm)                                                        \
+      launch_gemm<QB_, 1, CG_, 1, KR_, 0, MODE_>(maps, p, grid, smem, s);    \
+    else if (exact)                                                          \
+      launch_gemm<QB_, 1, CG_, 0, KR_, 0, MODE_>(maps, p, grid, smem, s);    \
+    else if (nbm)                                                            \
+      launch_gemm<QB_, 3, CG_, 1, KR_, 0, MODE_>(maps, p, grid, smem, s);    \
+    else                                                                     \
+      launch_gemm<QB_, 3, CG_, 0, KR_, 0, MODE_>(maps, p, grid, smem, s);    \
+    launched = true;                                                         \
+  }
+  MLXVS_GEMM_M(128, 2, 8, 1)
+  MLXVS_GEMM_M(128, 2, 8, 0)
+  MLXVS_GEMM_M(128, 2, 12, 0)
+  MLXVS_GEMM_M(128, 2, 16, 0)
+  MLXVS_GEMM_M(128, 2, 32, 0)
+#undef MLXVS_GEMM_M
+  require(launched, "[mlxvs_b200] no fused kernel for this shape");
+}
+
+// Large-k sizing: sample lists of LK_KG keys, 1 / LK_SAMPLE_DIV of the
+// base tiles sampled (at least LK_MIN_TILES tiles per sample).
+constexpr int LK_KG = 8;
+constexpr int LK_SAMPLE_DIV = 4;
+constexpr int LK_MIN_TILES = 16;
+
+// Exact search for k > 32 in three steps instead of per-query heaps:
+//   A. over G = ceil(k / LK_KG) disjoint strided samples of the base, the
+//      exact best ceil(k / G) of each (register lists, units that do not
+//      share lists or floors across samples); the smallest of the G worst
+//      keys has G * ceil(k / G) >= k rows at or above it: a floor;
+//   B. over the whole base, every candidate above that floor is kept
+//      (collect mode, per (split, query) buffers);
+//   C. the best k of the kept candidates, then keys -> ids / distances.
+// Returns false, having enqueued only harmless work, when a query kept more
+// candidates than its buffers hold (the caller then searches with heaps).
+bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exact, int nbm,
+                    int npa, int kchunks, bool fold, const __half* q_hi, const __half* q_lo,
+                    int64_t nq_pad, int d_pad, int mi, const float* qq, uint64_t* out_keys,
+                    int32_t* ids, float* dist, float out_scale, Scratch& sc, cudaStream_t s) {
+  DeviceInfo& dev = device_info();
+  const int k = p_in.k;
+  const int tiles = p_in.tiles;
+  const int G = (k + LK_KG - 1) / LK_KG;
+  const int kg = (k + G - 1) / G;
+  const int sample_tiles = std::max(LK_MIN_TILES * G, tiles / LK_SAMPLE_DIV);
+  if (k <= 32 || sample_tiles > tiles || nq_pad % 128 != 0) return false;
+  const int want = exact ? 4 : 2;
+  const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
+  const GemmShape sb = choose_shape(dev, npa, kchunks, 8, fold ? 1 : 0, nbm, want);
+  if (sa.qb != 128 || sa.cg != 2 || sa.kr == 0 || sb.qb != 128 || sb.cg != 2 || sb.kr != 8)
+    return false;
+  const int64_t nq = p_in.nq;
+  const int qblocks = (int)((nq + 127) / 128);
+  GemmMaps maps = maps_in;
+  maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, 128);
+  maps.a_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, 128);
+
+  // A: per-sample exact lists
+  KnnGemmParams pa = p_in;
+  pa.qblocks = qblocks;
+  pa.tiles = sample_tiles;
+  pa.splits = G;
+  pa.units = qblocks * G;
+  pa.k = kg;
+  pa.stages = sa.stages;
+  pa.a_stream = sa.a_stream;
+  pa.tile_stride = tiles / sample_tiles;
+  pa.no_inherit = 1;
+  pa.gfloor_split_stride = nq_pad;
+  pa.gfloor = sc.alloc<unsigned long long>((size_t)G * nq_pad);
+  CK(cudaMemsetAsync(pa.gfloor, 0, (size_t)G * nq_pad * 8, s));
+  pa.partial = sc.alloc<uint64_t>((size_t)G * nq_pad * kg);
+  pa.done = sc.alloc<int>((size_t)qblocks);
+  CK(cudaMemsetAsync(pa.done, 0, (size_t)qblocks * 4, s));
+  {
+    const GemmSmem lay = gemm_smem(128, npa, 2, kchunks, sa.stages, sa.a_stream, kg, fold, sa.kr,
+                                   nbm);
+    launch_shape(maps, pa, 128, 2, sa.kr, exact, nbm, 0, lay.total + 1024u,
+                 std::min(pa.units, dev.sms), s);
+  }
+  unsigned long long* floor = sc.alloc<unsigned long long>((size_t)nq_pad);
+  sample_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(pa.partial, G, nq_pad, kg,
+                                                                         nq, floor);
+  CK(cudaGetLastError());
+
+  // B: every candidate above the floor
+  KnnGemmParams pb = p_in;
+  pb.qblocks = qblocks;
+  pb.splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
+  pb.units = qblocks * pb.splits;
+  pb.k = 8;
+  pb.stages = sb.stages;
+  pb.a_stream = sb.a_stream;
+  pb.tile_stride = 1;
+  pb.no_inherit = 1;
+  pb.gfloor = floor;
+  pb.gfloor_split_stride = 0;
+  pb.done = pa.done;
+  pb.partial = pa.partial;  // not written in collect mode
+  // some 10 k candidates per query are expected above the floor; room for
+  // about five times that, spread over the splits
+  pb.collect_cap = (int)round_up(std::max<int64_t>(256, (int64_t)48 * k / pb.splits), 64);
+  pb.collect = sc.alloc<uint64_t>((size_t)pb.splits * nq_pad * pb.collect_cap);
+  pb.collect_count = sc.alloc<int32_t>((size_t)pb.splits * nq_pad);
+  {
+    const GemmSmem lay = gemm_smem(128, npa, 2, kchunks, sb.stages, sb.a_stream, 8, fold, 8, nbm);
+    launch_shape(maps, pb, 128, 2, 8, exact, nbm, 1, lay.total + 1024u,
+                 std::min(pb.units, dev.sms), s);
+  }
+
+  // C: the best k of the kept candidates
+  uint64_t* best = sc.alloc<uint64_t>((size_t)nq * k);
+  int32_t* overflow = sc.alloc<int32_t>(1);
+  CK(cudaMemsetAsync(overflow, 0, 4, s));
+  {
+    ProfScope prof("select_keys", s);
+    select_keys_kernel<<<(unsigned)nq, TOPK_THREADS, 0, s>>>(
+        pb.collect, pb.collect_count, pb.splits, nq_pad, pb.collect_cap, nq, k, best, overflow);
+    CK(cudaGetLastError());
+  }
+  int32_t h_overflow = 0;
+  CK(cudaMemcpyAsync(&h_overflow, overflow, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (h_overflow) return false;
+  launch_merge(best, 1, nq, nq, k, mi, qq, out_keys, ids, dist, s, out_scale);
+  return true;
 }
 
 // The exact k-NN of queries among base: keys [nq, k] (out_keys) and / or ids
@@ -430,8 +565,12 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.done = done;
   p.out_scale = out_scale;
   p.self_base = self_base;
+  p.tile_stride = 1;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
+  if (KR == 0 && large_k_search(maps, p, exact, nbm, npa, kchunks, fold, q_hi, q_lo, nq_pad,
+                                d_pad, mi, qq, out_keys, ids, dist, out_scale, sc, s))
+    return;
   const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k, fold, KR, nbm);
   const uint32_t smem = lay.total + 1024u;
   const int grid = std::min(units, dev.sms);
@@ -574,6 +713,7 @@ bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t
   p.out_scale = 1.0f;
   p.dot_offset = -0.5f * (float)bits;
   p.self_base = -1;
+  p.tile_stride = 1;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
   const GemmSmem lay = gemm_smem(sh.qb, 1, sh.cg, kchunks, sh.stages, sh.a_stream, k, 0, sh.kr, 1);

@@ -62,6 +62,21 @@ struct KnnGemmParams {
   // OP 1 (Hamming on +-1 int8 codes): score = dot / 2 + dot_offset, with
   // dot_offset = -bits / 2, i.e. minus the Hamming distance
   float dot_offset;
+  // base tile i of the units is tile i * tile_stride of the rows (1: all)
+  int32_t tile_stride;
+  // 0: a unit starts from the latest finished unit's lists of its query
+  // block; 1: every unit starts empty (its list is its own rows' best)
+  int32_t no_inherit;
+  // the shared floors of split s are gfloor + s * gfloor_split_stride (0:
+  // one floor per query for all units)
+  int64_t gfloor_split_stride;
+  // MODE 1 (collect): every candidate above the query's fixed floor goes to
+  // collect[(split * nq_pad + q) * collect_cap + i]; collect_count[split *
+  // nq_pad + q] receives how many there were (more than collect_cap means
+  // some were dropped and the caller must search another way)
+  uint64_t* collect;
+  int32_t* collect_count;
+  int32_t collect_cap;
   // >= 0: query q is the row with id self_base + q, which is never its own
   // neighbor (all_neighbors); -1: none
   int64_t self_base;
@@ -149,6 +164,8 @@ __device__ __forceinline__ void heap_replace_root(uint64_t* heap, int k, uint64_
 }
 
 struct EpiState {
+  uint64_t* cbuf;  // MODE 1: this query's candidate buffer of this unit
+  int* ccnt;       // MODE 1: its count (shared memory)
   uint32_t self_id;  // the query's own row id (all_neighbors), else 0xFFFFFFFF
   uint64_t floor;  // no candidate at or below this key can be in the result
   uint64_t gfl;    // the shared floor as last read or raised by this thread
@@ -238,7 +255,7 @@ __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
 
 // 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
 // with one compare when their max is below the floor, else offer each.
-template <int HS, int NBM, int KR, int OP, int RN>
+template <int HS, int NBM, int KR, int OP, int MODE, int RN>
 __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const float* nbs,
                                           int64_t col0, const KnnGemmParams& p, bool row_on,
                                           uint64_t* heap, uint64_t (&key)[KR > 0 ? KR : 1],
@@ -298,6 +315,14 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const 
           const float vj = sv[j * 32];
           const uint32_t id = id0 + (uint32_t)j;
           const uint64_t x = make_key(vj, id);
+          if constexpr (MODE == 1) {
+            // rows past nq (the last block's padding) have no buffer
+            if (st.cbuf != nullptr && x > st.floor && id != st.self_id) {
+              const int at = atomicAdd(st.ccnt, 1);
+              if (at < p.collect_cap) st.cbuf[at] = x;
+            }
+            continue;
+          }
           if (x > st.floor && id != st.self_id) {
             list_insert<KR>(key, x);
             if (key[0] > st.floor) st.floor = key[0];
@@ -310,7 +335,7 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const 
   }
 }
 
-template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0>
+template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0, int MODE = 0>
 __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     knn_gemm_topk_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                          const __grid_constant__ CUtensorMap tm_a_lo,
@@ -369,6 +394,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < CG * QB; i += blockDim.x) fl_all[i] = 0ull;
+  if (MODE == 1)  // the per-query candidate counters live where the lists meet
+    for (int i = threadIdx.x; i < QB; i += blockDim.x) reinterpret_cast<int*>(heap_all)[i] = 0;
   if (warp == L::MMA) {
     tmem_alloc(tmem_slot, 2 * GT_BN);
     tmem_relinquish();
@@ -442,10 +469,11 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             mbar_arrive_expect_tx(&full[stage], (uint32_t)(NPA * GT_BCHUNK) +
                                                     (p.a_stream ? a_bytes : 0u) +
                                                     (xk ? (uint32_t)GT_XCHUNK : 0u));
-            tma_load_2d(st, &tm_b_hi, &full[stage], kc * GT_KCH, t * GT_BN);
-            if (xk) tma_load_2d(st + x_in_stage, &tm_b_x, &full[stage], 0, t * GT_BN);
+            const int brow = t * p.tile_stride * GT_BN;
+            tma_load_2d(st, &tm_b_hi, &full[stage], kc * GT_KCH, brow);
+            if (xk) tma_load_2d(st + x_in_stage, &tm_b_x, &full[stage], 0, brow);
             if (NPASS == 3)
-              tma_load_2d(st + GT_BCHUNK, &tm_b_lo, &full[stage], kc * GT_KCH, t * GT_BN);
+              tma_load_2d(st + GT_BCHUNK, &tm_b_lo, &full[stage], kc * GT_KCH, brow);
             if (p.a_stream) {
               uint8_t* sa = st + NPA * GT_BCHUNK;
               tma_load_2d(sa, &tm_a_hi, &full[stage], kc * GT_KCH, qb * QB);
@@ -574,7 +602,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       // min-heap as written): the heap is full from its first tile, so its
       // root is a real floor and every improvement reaches the shared floor.
       // Column group 1 only takes the floor (its heap would duplicate them).
-      const int ds = *reinterpret_cast<volatile int*>(p.done + qb);
+      const int ds =
+          (MODE == 1 || p.no_inherit) ? 0 : *reinterpret_cast<volatile int*>(p.done + qb);
       __threadfence();
       uint64_t inherited = 0;
       if constexpr (KR > 0) {
@@ -604,16 +633,23 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       }
       EpiState st;
       st.self_id = (p.self_base >= 0 && q_ok) ? (uint32_t)(p.self_base + q) : 0xFFFFFFFFu;
-      st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q) : 0ull;
+      unsigned long long* gfl_q = p.gfloor + split * p.gfloor_split_stride + q;
+      st.cbuf = (MODE == 1 && q_ok)
+                    ? p.collect + ((size_t)split * p.nq_pad + q) * (size_t)p.collect_cap
+                    : nullptr;
+      st.ccnt = reinterpret_cast<int*>(heap_all) + (row_on ? row : 0);
+      st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(gfl_q) : 0ull;
       if (inherited > st.gfl) st.gfl = inherited;
       st.floor = st.gfl;
       st.thr = key_score(st.floor);
+      if (MODE == 1 && !q_ok) st.thr = INFINITY;  // padding rows collect nothing
       uint64_t gnext = st.gfl;
       float4 nbr[CW / 128];
       if (NBM == 0 && t0 < t1) {
 #pragma unroll
         for (int i = 0; i < CW / 128; ++i)
-          nbr[i] = __ldg(reinterpret_cast<const float4*>(p.nb + (int64_t)t0 * GT_BN + ch * CW) +
+          nbr[i] = __ldg(reinterpret_cast<const float4*>(
+                             p.nb + (int64_t)t0 * p.tile_stride * GT_BN + ch * CW) +
                          lane + 32 * i);
       }
       for (int t = t0; t < t1; ++t) {
@@ -629,7 +665,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
 #pragma unroll
           for (int i = 0; i < CW / 128; ++i)
             nbr[i] = __ldg(
-                reinterpret_cast<const float4*>(p.nb + (int64_t)(t + 1) * GT_BN + ch * CW) +
+                reinterpret_cast<const float4*>(
+                    p.nb + (int64_t)(t + 1) * p.tile_stride * GT_BN + ch * CW) +
                 lane + 32 * i);
         }
         if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.wait_ns)) {
@@ -639,7 +676,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         tc_fence_after();
         const uint32_t taddr =
             tmem_base + ((uint32_t)(rg * 32) << 16) + acc * GT_BN + (uint32_t)(ch * CW);
-        const int64_t col_base = (int64_t)t * GT_BN + ch * CW;
+        const int64_t col_base = (int64_t)t * p.tile_stride * GT_BN + ch * CW;
         if constexpr (KR >= 32) {
           // the long register lists leave room for 16-column loads only
           uint32_t ra[16], rb[16];
@@ -649,7 +686,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
           for (int c = 0; c < 2 * NCH; c += 2) {
             __syncwarp();
             tmem_ld16(taddr + (c + 1) * 16, rb);
-            epi_sub16<HS, NBM, KR, OP>(ra, 0, nbw + c * 16, col_base + c * 16, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 16, col_base + c * 16, p, row_on, heap, key, sv, st);
             __syncwarp();
             tmem_wait_ld_regs(rb);
             if (c + 2 < 2 * NCH) {
@@ -658,7 +695,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
               tc_fence_before();
               if (lane == 0) mbar_arrive(&acc_empty[acc]);
             }
-            epi_sub16<HS, NBM, KR, OP>(rb, 0, nbw + c * 16 + 16, col_base + c * 16 + 16, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP, MODE>(rb, 0, nbw + c * 16 + 16, col_base + c * 16 + 16, p, row_on, heap, key, sv, st);
             if (c + 2 < 2 * NCH) {
               __syncwarp();
               tmem_wait_ld_regs(ra);
@@ -672,8 +709,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          epi_sub16<HS, NBM, KR, OP>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR, OP>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP, MODE>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
           __syncwarp();
           tmem_wait_ld_regs(rb);
           if (c + 2 < NCH) {
@@ -683,8 +720,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
-          epi_sub16<HS, NBM, KR, OP>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR, OP>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP, MODE>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
+          epi_sub16<HS, NBM, KR, OP, MODE>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
           if (c + 2 < NCH) {
             __syncwarp();
             tmem_wait_ld_regs(ra);
@@ -693,7 +730,7 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         }
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;
-        if (CG == 2 && row_on) {
+        if (CG == 2 && row_on && MODE == 0) {
           // the other column group's floor for this query (a tile old at most)
           const uint64_t mine = KR > 0 ? key[0] : heap[0];
           fl_all[ch * QB + row] = mine;
@@ -717,13 +754,24 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             }
           }
           if (st.floor > st.gfl) {
-            atomicMax(p.gfloor + q, (unsigned long long)st.floor);
+            atomicMax(gfl_q, (unsigned long long)st.floor);
             st.gfl = st.floor;
           }
-          gnext = *reinterpret_cast<volatile unsigned long long*>(p.gfloor + q);
+          gnext = *reinterpret_cast<volatile unsigned long long*>(gfl_q);
         }
       }
       if (!ok) break;
+      if constexpr (MODE == 1) {
+        // both column groups have appended: the count goes out and the
+        // counter is cleared before either group starts its next unit
+        if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+        if (ch == 0 && row_on) {
+          if (q_ok) p.collect_count[(size_t)split * p.nq_pad + q] = *st.ccnt;
+          *st.ccnt = 0;
+        }
+        if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+        continue;
+      }
       if (CG == 2) {
         // the two column groups of each query meet: group 1's keys go into
         // group 0's selection, which is written out as the unit's list

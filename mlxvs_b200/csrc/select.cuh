@@ -177,6 +177,149 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams 
   }
 }
 
+// Large k, between the two passes: each of G disjoint samples of the base
+// (split g of the first pass) holds its exact best kg keys for query q, so
+// the smallest of their kg-th keys has at least G * kg >= k rows at or above
+// it and is a floor of the final k-th best.  floor[q] is that key minus one
+// (the key itself must pass), or 0 when some sample list is not full.
+__global__ void sample_floor_kernel(const uint64_t* __restrict__ lists, int32_t groups,
+                                    int64_t nq_pad, int32_t kg, int64_t nq,
+                                    unsigned long long* __restrict__ floor) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq_pad) return;
+  uint64_t f = ~0ull;
+  if (q < nq) {
+    for (int g = 0; g < groups; ++g) {
+      const uint64_t worst = lists[((size_t)g * nq_pad + q) * kg];  // lists are worst first
+      f = worst < f ? worst : f;
+    }
+  } else {
+    f = 0;
+  }
+  floor[q] = f == 0 ? 0ull : (unsigned long long)(f - 1);
+}
+
+// Large k, last step: the best k keys of the candidates the collecting pass
+// kept for each query (splits x cap keys, count[s * nq_pad + q] of them per
+// split), best first, 0-padded; a count above cap (candidates dropped) sets
+// *overflow.  One block per query: the radix select of topk_rows_kernel on
+// the keys themselves, then a bitonic sort by key.
+__global__ void __launch_bounds__(TOPK_THREADS)
+    select_keys_kernel(const uint64_t* __restrict__ cand, const int32_t* __restrict__ count,
+                       int32_t splits, int64_t nq_pad, int32_t cap, int64_t nq, int32_t k,
+                       uint64_t* __restrict__ out, int32_t* __restrict__ overflow) {
+  constexpr int WARPS = TOPK_THREADS / 32;
+  __shared__ uint32_t hist[WARPS][256];
+  __shared__ uint32_t suffix[256];
+  __shared__ uint32_t offs[65];
+  __shared__ unsigned long long s_prefix;
+  __shared__ uint32_t s_need, s_done;
+  __shared__ uint32_t taken_above, taken_equal;
+  __shared__ unsigned long long sel[TOPK_KMAX];
+  const int lid = threadIdx.x;
+  const int warp = lid >> 5;
+  const int64_t q = blockIdx.x;
+  if (q >= nq) return;
+  // prefix offsets of the splits' candidate runs (splits <= 64)
+  if (lid == 0) {
+    uint32_t acc = 0;
+    bool over = false;
+    for (int sp = 0; sp < splits; ++sp) {
+      offs[sp] = acc;
+      const int32_t c = count[(size_t)sp * nq_pad + q];
+      over |= c > cap;
+      acc += (uint32_t)(c < cap ? c : cap);
+    }
+    offs[splits] = acc;
+    if (over) atomicOr(overflow, 1);
+  }
+  __syncthreads();
+  const uint32_t total = offs[splits];
+  const uint32_t keff = (uint32_t)k < total ? (uint32_t)k : total;
+  auto cand_at = [&](uint32_t i) -> uint64_t {
+    int sp = 0;
+    while (offs[sp + 1] <= i) ++sp;
+    return cand[((size_t)sp * nq_pad + q) * cap + (i - offs[sp])];
+  };
+  uint64_t prefix = 0, mask = 0;
+  uint32_t need = keff;
+  if (keff > 0) {
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int i = lid; i < WARPS * 256; i += TOPK_THREADS) (&hist[0][0])[i] = 0u;
+      __syncthreads();
+      for (uint32_t i = lid; i < total; i += TOPK_THREADS) {
+        const uint64_t key = cand_at(i);
+        if ((key & mask) == prefix) atomicAdd(&hist[warp][(uint32_t)(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      uint32_t c = 0;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) c += hist[w][lid];
+      suffix[lid] = c;
+      __syncthreads();
+      for (int off = 1; off < 256; off <<= 1) {
+        const uint32_t add = lid + off < 256 ? suffix[lid + off] : 0u;
+        __syncthreads();
+        suffix[lid] += add;
+        __syncthreads();
+      }
+      const uint32_t at_or_above = suffix[lid];
+      const uint32_t above = at_or_above - c;
+      if (at_or_above >= need && above < need) {
+        s_prefix = prefix | ((uint64_t)lid << shift);
+        s_need = need - above;
+        s_done = (c == need - above) ? 1u : 0u;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      need = s_need;
+      mask |= 255ull << shift;
+      const bool done = s_done != 0;
+      __syncthreads();
+      if (done) break;
+    }
+  }
+  if (lid == 0) {
+    taken_above = 0;
+    taken_equal = 0;
+  }
+  for (int i = lid; i < TOPK_KMAX; i += TOPK_THREADS) sel[i] = 0ull;
+  __syncthreads();
+  const uint32_t n_above = keff - need;
+  if (keff > 0) {
+    for (uint32_t i = lid; i < total; i += TOPK_THREADS) {
+      const uint64_t key = cand_at(i);
+      const uint64_t mk = key & mask;
+      if (mk > prefix) {
+        sel[atomicAdd(&taken_above, 1u)] = key;
+      } else if (mk == prefix) {
+        const uint32_t at = atomicAdd(&taken_equal, 1u);
+        if (at < need) sel[n_above + at] = key;
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t size_pow2 = 1;
+  while (size_pow2 < keff) size_pow2 <<= 1;
+  for (uint32_t size = 2; size <= size_pow2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = lid; i < size_pow2; i += TOPK_THREADS) {
+        const uint32_t j = i ^ stride;
+        if (j > i) {
+          const bool forward = (i & size) == 0;
+          const uint64_t a = sel[i], b = sel[j];
+          if (forward != (a > b)) {
+            sel[i] = b;
+            sel[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = lid; i < k; i += TOPK_THREADS) out[(size_t)q * k + i] = (uint32_t)i < keff ? sel[i] : 0ull;
+}
+
 struct RefineParams {
   const float* dataset;       // [n][d]
   int64_t n;

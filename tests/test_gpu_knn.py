@@ -231,3 +231,32 @@ def test_golden_fixtures():
             assert dist.tolist() == case["distances"], case["name"]
         else:
             check_float(case["metric"], b, q, case["k"], ids, dist)
+
+
+@pytest.mark.parametrize("metric,k", [("l2", 33), ("l2", 100), ("inner_product", 100),
+                                      ("l2", 256), ("cosine", 64)])
+def test_large_k_sampled_floor_path(metric, k):
+    # k > 32 on a base large enough for the sampled-floor search (exact lists
+    # of 4+ disjoint samples -> a floor, every candidate above it kept, the
+    # best k selected); integer data bit-exact, unit rows within tolerance
+    if metric == "cosine":
+        b, q = data.lowrank_unit(80_000, 64, 16, seed=71, nq=300)
+        ids, dist = mv.brute_force_knn(b, q, k, metric)
+        check_float(metric, b, q, k, ids, dist)
+        return
+    b, q = data.gaussian_mixture_int(80_000, 128, 64, seed=72, nq=333)
+    ids, dist = mv.brute_force_knn(b, q, k, metric)
+    oids, odist = O.brute_force_knn(b, q, k, metric)
+    assert np.array_equal(ids, oids)
+    assert np.array_equal(dist, odist)
+
+
+def test_large_k_overflow_falls_back():
+    # identical rows: every row ties the floor, the kept candidates overflow
+    # their buffers and the search falls back to per-query heaps; the result
+    # is still the lowest ids
+    b = np.zeros((40_000, 32), np.float32)
+    q = np.zeros((50, 32), np.float32)
+    ids, dist = mv.brute_force_knn(b, q, 100, "l2")
+    assert (ids == np.arange(100)[None, :]).all()
+    assert (dist == 0).all()
