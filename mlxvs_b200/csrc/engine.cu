@@ -335,7 +335,8 @@ constexpr int LK_KG = 8;
 constexpr int LK_SAMPLE_DIV = 4;
 constexpr int LK_MIN_TILES = 16;
 
-// Exact search for k > 32 in three steps instead of per-query heaps:
+// Exact search for k > 16 in three steps instead of one pass with long
+// per-query lists (measured faster from k = 17 on):
 //   A. over G = ceil(k / LK_KG) disjoint strided samples of the base, the
 //      exact best ceil(k / G) of each (register lists, units that do not
 //      share lists or floors across samples); the smallest of the G worst
@@ -355,7 +356,7 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   const int G = (k + LK_KG - 1) / LK_KG;
   const int kg = (k + G - 1) / G;
   const int sample_tiles = std::max(LK_MIN_TILES * G, tiles / LK_SAMPLE_DIV);
-  if (k <= 32 || sample_tiles > tiles || nq_pad % 128 != 0) return false;
+  if (k <= 16 || sample_tiles > tiles || nq_pad % 128 != 0) return false;
   const int want = exact ? 4 : 2;
   const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
   const GemmShape sb = choose_shape(dev, npa, kchunks, 8, fold ? 1 : 0, nbm, want);
@@ -568,7 +569,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.tile_stride = 1;
   p.err = dev.err;
   p.wait_ns = WAIT_LIMIT_NS;
-  if (KR == 0 && large_k_search(maps, p, exact, nbm, npa, kchunks, fold, q_hi, q_lo, nq_pad,
+  if (k > 16 && large_k_search(maps, p, exact, nbm, npa, kchunks, fold, q_hi, q_lo, nq_pad,
                                 d_pad, mi, qq, out_keys, ids, dist, out_scale, sc, s))
     return;
   const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k, fold, KR, nbm);
