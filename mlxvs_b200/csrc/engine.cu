@@ -196,8 +196,7 @@ void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
   if (p.n_pad == 0) return;
   const int threads = 256;
   int64_t blocks = std::min<int64_t>((p.n_pad + 7) / 8, (int64_t)sms * 16);
-  bool vec = p.lo == nullptr && !p.cosine && p.d % 4 == 0 &&
-             (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+  bool vec = p.d % 4 == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
   ProfScope prof("prep", s);
   if (vec)
     prep_rows_vec4_kernel<<<(unsigned)blocks, threads, 0, s>>>(p);
@@ -349,14 +348,32 @@ constexpr int LK_MIN_TILES = 16;
 bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exact, int nbm,
                     int npa, int kchunks, bool fold, const __half* q_hi, const __half* q_lo,
                     int64_t nq_pad, int d_pad, int mi, const float* qq, uint64_t* out_keys,
-                    int32_t* ids, float* dist, float out_scale, Scratch& sc, cudaStream_t s) {
+                    int32_t* ids, float* dist, float out_scale, Scratch& sc, cudaStream_t s,
+                    RescoreParams* rescore = nullptr, float eps = 0.0f) {
   DeviceInfo& dev = device_info();
   const int k = p_in.k;
   const int tiles = p_in.tiles;
-  const int G = (k + LK_KG - 1) / LK_KG;
+  // G samples: ceil(k / LK_KG), or up to 3 times that when its units fill the
+  // SMs' waves much better (pass A takes about ceil(qblocks G / sms) / G of
+  // its sample's time; more samples also mean a lower floor, so a larger G
+  // must save a fifth of that)
+  const int qb_count = (int)((p_in.nq + 127) / 128);
+  const int g_min = (k + LK_KG - 1) / LK_KG;
+  auto wave_time = [&](int g) {
+    return (double)((qb_count * (int64_t)g + dev.sms - 1) / dev.sms) / g;
+  };
+  int G = g_min;
+  double best_t = wave_time(g_min);
+  for (int g = g_min + 1; g <= 3 * g_min; ++g) {
+    const double t = wave_time(g);
+    if (t < 0.8 * wave_time(g_min) && t < best_t * 0.999) {
+      best_t = t;
+      G = g;
+    }
+  }
   const int kg = (k + G - 1) / G;
   const int sample_tiles = std::max(LK_MIN_TILES * G, tiles / LK_SAMPLE_DIV);
-  if (k <= 16 || sample_tiles > tiles || nq_pad % 128 != 0) return false;
+  if ((k <= 16 && rescore == nullptr) || sample_tiles > tiles || nq_pad % 128 != 0) return false;
   const int want = exact ? 4 : 2;
   const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
   const GemmShape sb = choose_shape(dev, npa, kchunks, 8, fold ? 1 : 0, nbm, want);
@@ -395,6 +412,10 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   sample_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(pa.partial, G, nq_pad, kg,
                                                                          nq, floor);
   CK(cudaGetLastError());
+  if (rescore) {
+    margin_floor_kernel<<<(unsigned)((nq + 255) / 256), 256, 0, s>>>(floor, nq, eps);
+    CK(cudaGetLastError());
+  }
 
   // B: every candidate above the floor
   KnnGemmParams pb = p_in;
@@ -421,6 +442,20 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
                  std::min(pb.units, dev.sms), s);
   }
 
+  // (one fp16 pass) the kept candidates' exact scores
+  if (rescore) {
+    rescore->cand = pb.collect;
+    rescore->count = pb.collect_count;
+    rescore->splits = pb.splits;
+    rescore->nq = nq;
+    rescore->nq_pad = nq_pad;
+    rescore->cap = pb.collect_cap;
+    const int64_t pairs = (int64_t)pb.splits * nq;
+    ProfScope prof("rescore", s);
+    rescore_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(*rescore);
+    CK(cudaGetLastError());
+  }
+
   // C: the best k of the kept candidates
   uint64_t* best = sc.alloc<uint64_t>((size_t)nq * k);
   int32_t* overflow = sc.alloc<int32_t>(1);
@@ -437,6 +472,49 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   if (h_overflow) return false;
   launch_merge(best, 1, nq, nq, k, mi, qq, out_keys, ids, dist, s, out_scale);
   return true;
+}
+
+// Inexact float operands: one fp16 pass with a margin and exact rescoring
+// (large_k_search in its rescoring form).  b_hi / q_hi hold the scaled
+// fp16 operands, nb the scaled |b|^2 (L2), qq the unscaled |q|^2 (L2).
+bool approx_search(const float* base, int64_t n, const float* queries, int64_t nq, int d, int k,
+                   int mi, int64_t id_offset, int64_t self_base, const __half* b_hi,
+                   const __half* q_hi, const float* nb, const float* qq, int64_t n_pad,
+                   int64_t nq_pad, int d_pad, int kchunks, int nbm, float eps,
+                   uint64_t* out_keys, int32_t* ids, float* dist, Scratch& sc, cudaStream_t s) {
+  DeviceInfo& dev = device_info();
+  if (!(eps < INFINITY)) return false;
+  GemmMaps maps;
+  maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, 128);
+  maps.a_lo = maps.a_hi;
+  maps.b_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  maps.b_lo = maps.b_hi;
+  maps.b_x = maps.b_hi;
+  KnnGemmParams p{};
+  p.qblocks = (int)((nq + 127) / 128);
+  p.tiles = (int)(n_pad / GT_BN);
+  p.kchunks = kchunks;
+  p.k = k;
+  p.extra = 0;
+  p.n_valid = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.id_offset = id_offset;
+  p.nb = nb;
+  p.out_scale = 1.0f;
+  p.self_base = self_base;
+  p.tile_stride = 1;
+  p.err = dev.err;
+  p.wait_ns = WAIT_LIMIT_NS;
+  RescoreParams rs{};
+  rs.base = base;
+  rs.queries = queries;
+  rs.n = n;
+  rs.d = d;
+  rs.id_offset = id_offset;
+  rs.metric = mi;
+  return large_k_search(maps, p, true, nbm, 1, kchunks, false, q_hi, nullptr, nq_pad, d_pad, mi,
+                        qq, out_keys, ids, dist, 1.0f, sc, s, &rs, eps);
 }
 
 // The exact k-NN of queries among base: keys [nq, k] (out_keys) and / or ids
@@ -483,10 +561,12 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   uint32_t* flags = sc.alloc<uint32_t>(8);
   CK(cudaMemsetAsync(flags, 0, 32, s));
 
+  // flags[5], flags[6]: the largest squared row norm of the base and query
+  // operands (before scaling), for the error bound of one fp16 pass
   PrepParams pb{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, 1.0f, b_hi, nullptr,
-                nb, l2 ? 1.0f : 0.0f, INFINITY, flags, b_x, flags + 4};
+                nb, l2 ? 1.0f : 0.0f, INFINITY, flags, b_x, flags + 4, flags + 5};
   PrepParams pq{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, 1.0f, q_hi,
-                nullptr, qq, 1.0f, 0.0f, flags + 2, nullptr, nullptr};
+                nullptr, qq, 1.0f, 0.0f, flags + 2, nullptr, nullptr, flags + 6};
   launch_prep(pb, dev.sms, s);
   launch_prep(pq, dev.sms, s);
   uint32_t hflags[8];
@@ -513,6 +593,36 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
     };
     const int eb = scale_exp(amax_b), eq = scale_exp(amax_q);
     const float sb = std::ldexp(1.0f, eb), sq = std::ldexp(1.0f, eq);
+    if (n_pad / GT_BN >= 64) {
+      // one fp16 pass of the scaled operands (hi only), every candidate
+      // within twice its error bound of a sampled floor kept, then exact
+      // float32 scores; the three-pass split below when buffers overflow
+      PrepParams pb1{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, nullptr,
+                     nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr, nullptr,
+                     nullptr};
+      PrepParams pq1{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, sq, q_hi,
+                     nullptr, nullptr, 0.0f, 0.0f, nullptr, nullptr, nullptr};
+      launch_prep(pb1, dev.sms, s);
+      launch_prep(pq1, dev.sms, s);
+      float nb2, nq2;
+      std::memcpy(&nb2, &hflags[5], 4);
+      std::memcpy(&nq2, &hflags[6], 4);
+      // |fp16 dot - exact dot| <= (2u + u^2 + (d + 16) 2^-24) |a| |b| (rounding
+      // of both operands, u = 2^-11, and of the fp32 accumulation) plus
+      // 2^-25 sqrt(d) (|a| + |b|) for operands in fp16's subnormal range; L2
+      // adds the rounding of "dot - |b|^2"; doubled for safety
+      const double na = std::sqrt((double)nq2) * 1.001 * std::ldexp(1.0, eq);
+      const double nbn = std::sqrt((double)nb2) * 1.001 * std::ldexp(1.0, eb);
+      const double u = std::ldexp(1.0, -11);
+      double e = (2 * u + u * u + (d + 16) * std::ldexp(1.0, -24)) * na * nbn +
+                 std::ldexp(1.0, -25) * std::sqrt((double)d) * (na + nbn);
+      if (l2) e += std::ldexp(1.0, -23) * (na * nbn + (double)nb2 * 1.001 * std::ldexp(1.0, eb + eq));
+      const float eps = (float)(2.0 * e);
+      if (approx_search(base, n, queries, nq, d, k, mi, id_offset, self_base, b_hi, q_hi, nb, qq,
+                        n_pad, nq_pad, d_pad, kchunks, l2 ? 0 : 1, eps, out_keys, ids, dist, sc,
+                        s))
+        return;
+    }
     b_lo = sc.alloc<__half>((size_t)n_pad * d_pad);
     q_lo = sc.alloc<__half>((size_t)nq_pad * d_pad);
     PrepParams pb2{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, b_lo,

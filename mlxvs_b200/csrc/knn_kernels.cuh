@@ -41,6 +41,9 @@ struct PrepParams {
   uint32_t* flags;
   __half* xp;
   uint32_t* fold_flag;
+  // may be null: receives the largest sum(w^2) of a row (w before the
+  // power-of-two scale), as float bits (for error bounds of fp16 scores)
+  uint32_t* rownorm_max;
 };
 
 #ifdef __CUDACC__
@@ -104,12 +107,14 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     }
     ss = warp_sum(ss);
     float f = p.mul;
+    float wss = 0.0f;
     if (p.cosine) {
       float den = fmaxf(sqrtf(ss), 1e-30f);
       // x / den as the reference divides; mul and scale are powers of two
       for (int c = lane; c < p.d_pad; c += 32) {
         float y = c < p.d ? __ldg(xr + c) / den : 0.0f;
         float w = y * f;
+        wss = fmaf(w, w, wss);
         amax = fmaxf(amax, fabsf(w));
         w *= p.scale;
         __half h = __float2half_rn(w);
@@ -123,6 +128,7 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     } else {
       for (int c = lane; c < p.d_pad; c += 32) {
         float w = c < p.d ? __ldg(xr + c) * f : 0.0f;
+        wss = fmaf(w, w, wss);
         amax = fmaxf(amax, fabsf(w));
         w *= p.scale;
         __half h = __float2half_rn(w);
@@ -136,6 +142,10 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     }
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
+    if (p.rownorm_max) {
+      wss = warp_sum(wss);
+      if (lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wss));
+    }
   }
   if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {
@@ -148,8 +158,9 @@ __global__ void prep_rows_kernel(const PrepParams p) {
   }
 }
 
-// Vectorized prep for d % 4 == 0 and 16-byte aligned rows, one-pass only
-// (lo == nullptr, cosine == 0): the benchmark's hot case.
+// The same for d % 4 == 0 and 16-byte aligned rows, four values per lane
+// and step (float4 loads, 8-byte half stores).  Cosine rows take one more
+// pass over the row for the norm first.
 __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -160,18 +171,41 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
        row += warps) {
     uint2* hrow = reinterpret_cast<uint2*>(p.hi + (size_t)row * p.d_pad);
+    uint2* lrow = p.lo ? reinterpret_cast<uint2*>(p.lo + (size_t)row * p.d_pad) : nullptr;
     if (row >= p.n) {
-      for (int c = lane; c < dp4; c += 32) hrow[c] = make_uint2(0u, 0u);
+      for (int c = lane; c < dp4; c += 32) {
+        hrow[c] = make_uint2(0u, 0u);
+        if (lrow) lrow[c] = make_uint2(0u, 0u);
+      }
       if (p.norm_out && lane == 0) p.norm_out[row] = p.pad_norm;
       if (p.xp && lane == 0) write_pieces(p.xp, row, 0.0f, false);
       continue;
     }
     const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)row * p.d);
     float ss = 0.0f;
+    float den = 1.0f;
+    if (p.cosine) {
+      for (int c = lane; c < d4; c += 32) {
+        const float4 v = __ldg(xr + c);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      den = fmaxf(sqrtf(ss), 1e-30f);
+    }
+    float ss_main = 0.0f, wss = 0.0f;
     for (int c = lane; c < dp4; c += 32) {
       float4 v = c < d4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      if (p.cosine) {
+        // x / den as the reference divides
+        v.x = v.x / den;
+        v.y = v.y / den;
+        v.z = v.z / den;
+        v.w = v.w / den;
+      } else {
+        ss_main += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
       float w0 = v.x * p.mul, w1 = v.y * p.mul, w2 = v.z * p.mul, w3 = v.w * p.mul;
+      wss += w0 * w0 + w1 * w1 + w2 * w2 + w3 * w3;
       amax = fmaxf(amax, fmaxf(fmaxf(fabsf(w0), fabsf(w1)), fmaxf(fabsf(w2), fabsf(w3))));
       w0 *= p.scale;
       w1 *= p.scale;
@@ -179,16 +213,30 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
       w3 *= p.scale;
       __half2 h01 = __floats2half2_rn(w0, w1);
       __half2 h23 = __floats2half2_rn(w2, w3);
-      float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
-      if (b01.x != w0 || b01.y != w1 || b23.x != w2 || b23.y != w3) inexact = 1;
+      const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
       uint2 out;
       out.x = *reinterpret_cast<uint32_t*>(&h01);
       out.y = *reinterpret_cast<uint32_t*>(&h23);
       hrow[c] = out;
+      if (lrow) {
+        __half2 l01 = __floats2half2_rn(w0 - b01.x, w1 - b01.y);
+        __half2 l23 = __floats2half2_rn(w2 - b23.x, w3 - b23.y);
+        uint2 lo;
+        lo.x = *reinterpret_cast<uint32_t*>(&l01);
+        lo.y = *reinterpret_cast<uint32_t*>(&l23);
+        lrow[c] = lo;
+      } else if (b01.x != w0 || b01.y != w1 || b23.x != w2 || b23.y != w3) {
+        inexact = 1;
+      }
     }
-    ss = warp_sum(ss);
+    if (!p.cosine) ss = ss_main;
+    if (!p.cosine) ss = warp_sum(ss);
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
+    if (p.rownorm_max) {
+      wss = warp_sum(wss);
+      if (lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wss));
+    }
   }
   if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {

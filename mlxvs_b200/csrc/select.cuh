@@ -199,6 +199,83 @@ __global__ void sample_floor_kernel(const uint64_t* __restrict__ lists, int32_t 
   floor[q] = f == 0 ? 0ull : (unsigned long long)(f - 1);
 }
 
+// One fp16 pass on inexact operands: lowers each query's floor (a key F - 1,
+// from sample_floor_kernel) by 2 eps, eps bounding |fp16 score - exact
+// score| in the same units: every row of the exact best k then scores at
+// least F - 2 eps in the fp16 pass.  The new floor is the key of that score
+// (rounded down) with the lowest id part.
+__global__ void margin_floor_kernel(unsigned long long* __restrict__ floor, int64_t nq,
+                                    float eps) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const uint64_t f = floor[q];
+  if (f == 0) return;
+  const float s = __fsub_rd(key_score(f + 1), 2.0f * eps);
+  floor[q] = (unsigned long long)order_bits(s) << 32;
+}
+
+struct RescoreParams {
+  const float* base;      // [n][d] float32, the caller's rows
+  const float* queries;   // [nq][d]
+  int64_t n;
+  int32_t d;
+  int64_t id_offset;      // ids in the keys are id_offset + row
+  int32_t metric;         // 0 inner product, 1 L2, 2 cosine
+  uint64_t* cand;         // [splits][nq_pad][cap] keys, rewritten in place
+  const int32_t* count;   // [splits][nq_pad]
+  int32_t splits;
+  int64_t nq;
+  int64_t nq_pad;
+  int32_t cap;
+};
+
+// The kept candidates' keys with exact float32 scores in the reference's
+// form (src/knn.cpp:111-116: L2 2 q.b - |b|^2, inner product q.b, cosine
+// q.b / (max(|q|, 1e-30) max(|b|, 1e-30))), one warp per (split, query)
+// walking its candidates; the row is read from the caller's float32 base.
+__global__ void rescore_kernel(RescoreParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= (int64_t)p.splits * p.nq) return;
+  const int32_t sp = (int32_t)(pair / p.nq);
+  const int64_t q = pair - (int64_t)sp * p.nq;
+  int32_t cnt = p.count[(size_t)sp * p.nq_pad + q];
+  cnt = cnt < p.cap ? cnt : p.cap;
+  if (cnt <= 0) return;
+  const float* x = p.queries + q * p.d;
+  float qq = 0.0f;
+  if (p.metric == 2) {
+    for (int j = lane; j < p.d; j += 32) qq = fmaf(x[j], x[j], qq);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) qq += __shfl_xor_sync(0xffffffffu, qq, off);
+  }
+  uint64_t* keys = p.cand + ((size_t)sp * p.nq_pad + q) * (size_t)p.cap;
+  for (int32_t i = 0; i < cnt; ++i) {
+    const uint64_t key = keys[i];
+    const uint32_t id = ~(uint32_t)key;
+    const float* r = p.base + ((int64_t)id - p.id_offset) * p.d;
+    float dot = 0.0f, rr = 0.0f;
+    for (int j = lane; j < p.d; j += 32) {
+      const float a = __ldg(r + j);
+      dot = fmaf(a, x[j], dot);
+      rr = fmaf(a, a, rr);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      rr += __shfl_xor_sync(0xffffffffu, rr, off);
+    }
+    float sc;
+    if (p.metric == 1)
+      sc = 2.0f * dot - rr;
+    else if (p.metric == 2)
+      sc = dot / (fmaxf(sqrtf(qq), 1e-30f) * fmaxf(sqrtf(rr), 1e-30f));
+    else
+      sc = dot;
+    if (lane == 0) keys[i] = make_key(sc, id);
+  }
+}
+
 // Large k, last step: the best k keys of the candidates the collecting pass
 // kept for each query (splits x cap keys, count[s * nq_pad + q] of them per
 // split), best first, 0-padded; a count above cap (candidates dropped) sets

@@ -260,3 +260,28 @@ def test_large_k_overflow_falls_back():
     ids, dist = mv.brute_force_knn(b, q, 100, "l2")
     assert (ids == np.arange(100)[None, :]).all()
     assert (dist == 0).all()
+
+
+@pytest.mark.parametrize("metric,k", [("l2", 10), ("inner_product", 1), ("cosine", 10),
+                                      ("cosine", 50), ("l2", 128)])
+def test_inexact_floats_one_pass_with_rescoring(metric, k):
+    # general float32 rows on a base of 64+ tiles: one fp16 pass keeps every
+    # candidate within its error bound of a sampled floor, exact float32
+    # scores decide (recall 1, distances within 1e-4)
+    b, q = data.lowrank_unit(70_000, 256, 32, seed=81, nq=400)
+    if metric != "cosine":
+        b = b * np.float32(3.7)
+        q = q * np.float32(0.6)
+    ids, dist = mv.brute_force_knn(b, q, k, metric)
+    check_float(metric, b, q, k, ids, dist)
+
+
+def test_inexact_floats_near_ties():
+    # rows that differ by far less than the fp16 rounding: the margin keeps
+    # them all, the exact scores order them
+    rng = np.random.default_rng(82)
+    b = data.normal_rows(40_000, 64, seed=83)
+    b[20_000:] = b[:20_000] + rng.standard_normal((20_000, 64)).astype(np.float32) * 1e-5
+    q = b[:300] + rng.standard_normal((300, 64)).astype(np.float32) * 1e-3
+    ids, dist = mv.brute_force_knn(b, q, 10, "l2")
+    check_float("l2", b, q, 10, ids, dist)
