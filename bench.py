@@ -45,6 +45,12 @@ WORKLOADS = {
     "knn-cos-1m-1536": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
                             metric="cosine", rank=64,
                             desc="config 2: 1M x 1536 fp32 unit rows, cosine, k=10"),
+    # config 2 with float16 storage (the rows rounded to fp16, computed in
+    # fp32 after the upcast, as the reference does with an f16 array)
+    "knn-cos-1m-1536-f16": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
+                                metric="cosine", rank=64, f16=True,
+                                desc="config 2 with float16 storage: 1M x 1536 unit rows "
+                                     "rounded to fp16, cosine, k=10"),
     # the exact k-NN graph (all_neighbors, one cluster,
     # brute force) of the config-1 generator's 1M rows, k=32 (the reference
     # searches k + 1 = 33 and drops each row itself)
@@ -166,6 +172,9 @@ def make_inputs(w, device, seed=0):
     elif w["kind"] == "knn-unit":
         base = gen_unit_torch(w["n"], w["d"], w["rank"], seed, device)
         q = gen_unit_torch(w["nq"], w["d"], w["rank"], seed + 1, device)
+        if w.get("f16"):
+            base = base.half().float()
+            q = q.half().float()
     else:
         base = gen_codes_torch(w["n"], w["bytes"], w["prototypes"], w["flip"], seed, device)
         q = gen_codes_torch(w["nq"], w["bytes"], w["prototypes"], w["flip"], seed + 1, device)

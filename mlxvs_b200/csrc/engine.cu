@@ -281,7 +281,8 @@ struct GemmShape {
 GemmShape choose_shape(const DeviceInfo& dev, int npa, int kchunks, int k, int extra, int nbm,
                        int want_stages) {
   const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
-  const int kr = k <= 8 ? 8 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0)));
+  const int kr =
+      k <= 8 ? 8 : (k <= 10 ? 10 : (k <= 12 ? 12 : (k <= 16 ? 16 : (k <= 32 ? 32 : 0))));
   struct Shape { int qb, cg, kr, min_st; };
   const Shape order[] = {{128, 2, kr, want_stages}, {128, 2, kr, 2},
                          {128, 2, 0, want_stages},  {128, 2, 0, 2},
@@ -321,6 +322,7 @@ void launch_shape(const GemmMaps& maps, const KnnGemmParams& p, int qb, int cg, 
   }
   MLXVS_GEMM_M(128, 2, 8, 1)
   MLXVS_GEMM_M(128, 2, 8, 0)
+  MLXVS_GEMM_M(128, 2, 10, 0)
   MLXVS_GEMM_M(128, 2, 12, 0)
   MLXVS_GEMM_M(128, 2, 16, 0)
   MLXVS_GEMM_M(128, 2, 32, 0)
@@ -697,6 +699,7 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
       launch_gemm<QB_, 3, CG_, 0, KR_>(maps, p, grid, smem, s);           \
   }
   MLXVS_GEMM(128, 2, 8)
+  MLXVS_GEMM(128, 2, 10)
   MLXVS_GEMM(128, 2, 12)
   MLXVS_GEMM(128, 2, 16)
   MLXVS_GEMM(128, 2, 32)
@@ -837,6 +840,7 @@ bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t
     launched = true;                                                   \
   }
   MLXVS_HGEMM(128, 2, 8)
+  MLXVS_HGEMM(128, 2, 10)
   MLXVS_HGEMM(128, 2, 12)
   MLXVS_HGEMM(128, 2, 16)
   MLXVS_HGEMM(128, 2, 32)

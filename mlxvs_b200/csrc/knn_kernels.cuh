@@ -86,6 +86,7 @@ __global__ void prep_rows_kernel(const PrepParams p) {
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   uint32_t inexact = 0, unfoldable = 0;
   float amax = 0.0f;
+  float wmax = 0.0f;  // the largest sum(w^2) of this warp's rows
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
        row += warps) {
     __half* hrow = p.hi + (size_t)row * p.d_pad;
@@ -142,11 +143,10 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     }
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
-    if (p.rownorm_max) {
-      wss = warp_sum(wss);
-      if (lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wss));
-    }
+    if (p.rownorm_max) wmax = fmaxf(wmax, warp_sum(wss));
   }
+  // one atomic per warp (a million rows on one address would serialize)
+  if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
   if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {
     inexact = __any_sync(0xffffffffu, inexact);
@@ -166,6 +166,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   uint32_t inexact = 0, unfoldable = 0;
   float amax = 0.0f;
+  float wmax = 0.0f;  // the largest sum(w^2) of this warp's rows
   const int d4 = p.d >> 2;
   const int dp4 = p.d_pad >> 2;
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
@@ -233,11 +234,10 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
     if (!p.cosine) ss = warp_sum(ss);
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
-    if (p.rownorm_max) {
-      wss = warp_sum(wss);
-      if (lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wss));
-    }
+    if (p.rownorm_max) wmax = fmaxf(wmax, warp_sum(wss));
   }
+  // one atomic per warp (a million rows on one address would serialize)
+  if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
   if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
   if (p.flags) {
     inexact = __any_sync(0xffffffffu, inexact);
