@@ -108,14 +108,12 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     }
     ss = warp_sum(ss);
     float f = p.mul;
-    float wss = 0.0f;
     if (p.cosine) {
       float den = fmaxf(sqrtf(ss), 1e-30f);
       // x / den as the reference divides; mul and scale are powers of two
       for (int c = lane; c < p.d_pad; c += 32) {
         float y = c < p.d ? __ldg(xr + c) / den : 0.0f;
         float w = y * f;
-        wss = fmaf(w, w, wss);
         amax = fmaxf(amax, fabsf(w));
         w *= p.scale;
         __half h = __float2half_rn(w);
@@ -129,7 +127,6 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     } else {
       for (int c = lane; c < p.d_pad; c += 32) {
         float w = c < p.d ? __ldg(xr + c) * f : 0.0f;
-        wss = fmaf(w, w, wss);
         amax = fmaxf(amax, fabsf(w));
         w *= p.scale;
         __half h = __float2half_rn(w);
@@ -143,7 +140,10 @@ __global__ void prep_rows_kernel(const PrepParams p) {
     }
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
-    if (p.rownorm_max) wmax = fmaxf(wmax, warp_sum(wss));
+    // sum(w^2) = mul^2 |x|^2 exactly (mul is a power of two); unit rows
+    // (cosine) have norm at most 1 up to rounding, which the caller's
+    // safety factor covers
+    if (p.rownorm_max) wmax = fmaxf(wmax, p.cosine ? p.mul * p.mul : ss * p.mul * p.mul);
   }
   // one atomic per warp (a million rows on one address would serialize)
   if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
@@ -161,6 +161,9 @@ __global__ void prep_rows_kernel(const PrepParams p) {
 // The same for d % 4 == 0 and 16-byte aligned rows, four values per lane
 // and step (float4 loads, 8-byte half stores).  Cosine rows take one more
 // pass over the row for the norm first.
+// GENERAL = false compiles the plain case only (no cosine, no split plane):
+// fewer registers, more rows in flight per SM.
+template <bool GENERAL>
 __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -172,7 +175,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
        row += warps) {
     uint2* hrow = reinterpret_cast<uint2*>(p.hi + (size_t)row * p.d_pad);
-    uint2* lrow = p.lo ? reinterpret_cast<uint2*>(p.lo + (size_t)row * p.d_pad) : nullptr;
+    uint2* lrow = (GENERAL && p.lo) ? reinterpret_cast<uint2*>(p.lo + (size_t)row * p.d_pad) : nullptr;
     if (row >= p.n) {
       for (int c = lane; c < dp4; c += 32) {
         hrow[c] = make_uint2(0u, 0u);
@@ -185,7 +188,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
     const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)row * p.d);
     float ss = 0.0f;
     float den = 1.0f;
-    if (p.cosine) {
+    if (GENERAL && p.cosine) {
       for (int c = lane; c < d4; c += 32) {
         const float4 v = __ldg(xr + c);
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -193,10 +196,10 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
       ss = warp_sum(ss);
       den = fmaxf(sqrtf(ss), 1e-30f);
     }
-    float ss_main = 0.0f, wss = 0.0f;
+    float ss_main = 0.0f;
     for (int c = lane; c < dp4; c += 32) {
       float4 v = c < d4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (p.cosine) {
+      if (GENERAL && p.cosine) {
         // x / den as the reference divides
         v.x = v.x / den;
         v.y = v.y / den;
@@ -206,7 +209,6 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
         ss_main += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
       }
       float w0 = v.x * p.mul, w1 = v.y * p.mul, w2 = v.z * p.mul, w3 = v.w * p.mul;
-      wss += w0 * w0 + w1 * w1 + w2 * w2 + w3 * w3;
       amax = fmaxf(amax, fmaxf(fmaxf(fabsf(w0), fabsf(w1)), fmaxf(fabsf(w2), fabsf(w3))));
       w0 *= p.scale;
       w1 *= p.scale;
@@ -219,7 +221,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
       out.x = *reinterpret_cast<uint32_t*>(&h01);
       out.y = *reinterpret_cast<uint32_t*>(&h23);
       hrow[c] = out;
-      if (lrow) {
+      if (GENERAL && lrow) {
         __half2 l01 = __floats2half2_rn(w0 - b01.x, w1 - b01.y);
         __half2 l23 = __floats2half2_rn(w2 - b23.x, w3 - b23.y);
         uint2 lo;
@@ -230,11 +232,13 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
         inexact = 1;
       }
     }
-    if (!p.cosine) ss = ss_main;
-    if (!p.cosine) ss = warp_sum(ss);
+    if (!(GENERAL && p.cosine)) ss = warp_sum(ss_main);
     if (p.norm_out && lane == 0) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss * p.norm_scale;
     if (p.xp && lane == 0) unfoldable |= write_pieces(p.xp, row, ss, true);
-    if (p.rownorm_max) wmax = fmaxf(wmax, warp_sum(wss));
+    // sum(w^2) = mul^2 |x|^2 exactly (mul is a power of two); unit rows
+    // (cosine) have norm at most 1 up to rounding, which the caller's
+    // safety factor covers
+    if (p.rownorm_max) wmax = fmaxf(wmax, (GENERAL && p.cosine) ? p.mul * p.mul : ss * p.mul * p.mul);
   }
   // one atomic per warp (a million rows on one address would serialize)
   if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
