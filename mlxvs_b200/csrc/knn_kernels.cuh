@@ -172,8 +172,21 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   float wmax = 0.0f;  // the largest sum(w^2) of this warp's rows
   const int d4 = p.d >> 2;
   const int dp4 = p.d_pad >> 2;
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.n_pad;
-       row += warps) {
+  const int64_t row0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  // plain case: each lane's first four values of the next row are loaded
+  // one row ahead, so two loads per warp are in flight
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 ahead = (!GENERAL && row0 < p.n && lane < d4)
+                     ? __ldg(reinterpret_cast<const float4*>(p.x + (size_t)row0 * p.d) + lane)
+                     : zero4;
+  for (int64_t row = row0; row < p.n_pad; row += warps) {
+    const float4 first = ahead;
+    if (!GENERAL) {
+      const int64_t nr = row + warps;
+      ahead = (nr < p.n && lane < d4)
+                  ? __ldg(reinterpret_cast<const float4*>(p.x + (size_t)nr * p.d) + lane)
+                  : zero4;
+    }
     uint2* hrow = reinterpret_cast<uint2*>(p.hi + (size_t)row * p.d_pad);
     uint2* lrow = (GENERAL && p.lo) ? reinterpret_cast<uint2*>(p.lo + (size_t)row * p.d_pad) : nullptr;
     if (row >= p.n) {
@@ -198,7 +211,7 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
     }
     float ss_main = 0.0f;
     for (int c = lane; c < dp4; c += 32) {
-      float4 v = c < d4 ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 v = (!GENERAL && c == lane) ? first : (c < d4 ? __ldg(xr + c) : zero4);
       if (GENERAL && p.cosine) {
         // x / den as the reference divides
         v.x = v.x / den;
