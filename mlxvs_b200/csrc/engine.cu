@@ -505,7 +505,6 @@ bool approx_search(const float* base, int64_t n, const float* queries, int64_t n
   p.nq_pad = nq_pad;
   p.id_offset = id_offset;
   p.nb = nb;
-  p.out_scale = 1.0f;
   p.self_base = self_base;
   p.tile_stride = 1;
   p.err = dev.err;
@@ -678,7 +677,6 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   p.partial = partial;
   p.gfloor = gfloor;
   p.done = done;
-  p.out_scale = out_scale;
   p.self_base = self_base;
   p.tile_stride = 1;
   p.err = dev.err;
@@ -826,7 +824,6 @@ bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t
   p.partial = partial;
   p.gfloor = gfloor;
   p.done = done;
-  p.out_scale = 1.0f;
   p.dot_offset = -0.5f * (float)bits;
   p.self_base = -1;
   p.tile_stride = 1;

@@ -58,7 +58,6 @@ struct KnnGemmParams {
   uint64_t* partial;               // [splits][nq_pad][k] keys
   unsigned long long* gfloor;      // [nq_pad] shared floor keys (0 = none)
   int* done;                       // [qblocks] 1 + the latest split whose lists are written
-  float out_scale;                 // partial scores are written as score * out_scale
   // OP 1 (Hamming on +-1 int8 codes): score = dot / 2 + dot_offset, with
   // dot_offset = -bits / 2, i.e. minus the Hamming distance
   float dot_offset;
