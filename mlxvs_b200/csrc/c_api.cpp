@@ -96,6 +96,28 @@ cudaStream_t thread_stream() {
   return s;
 }
 
+// A second stream per thread and device, for host-to-device copies that
+// overlap the search.
+cudaStream_t thread_copy_stream() {
+  thread_local cudaStream_t s = nullptr;
+  thread_local int dev = -1;
+  int cur = 0;
+  ck(cudaGetDevice(&cur), "cudaGetDevice");
+  if (s == nullptr || dev != cur) {
+    ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+    dev = cur;
+  }
+  return s;
+}
+
+// Base chunks copied and searched one after another (the copies of later
+// chunks overlap the searches of earlier ones): 1 below 2^18 rows, else up
+// to 8 chunks of at least 2^17 rows.
+int copy_chunks(int64_t n) {
+  if (n < (1LL << 18)) return 1;
+  return (int)std::min<int64_t>(8, n >> 17);
+}
+
 }  // namespace
 
 extern "C" {
@@ -123,9 +145,45 @@ int mlxvs_brute_force_knn(const float* base, int64_t n, const float* queries, in
     float* dq = static_cast<float*>(buf.alloc(qbytes));
     int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
     float* ddist = distances ? static_cast<float*>(buf.alloc(count * sizeof(float))) : nullptr;
-    if (bbytes) ck(cudaMemcpyAsync(db, base, bbytes, cudaMemcpyHostToDevice, s), "copy base");
     ck(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, s), "copy queries");
-    mlxvs_b200::brute_force_knn(db, n, dq, nq, d, k, m, dids, ddist, s);
+    const int chunks = copy_chunks(n);
+    if (chunks == 1) {
+      if (bbytes) ck(cudaMemcpyAsync(db, base, bbytes, cudaMemcpyHostToDevice, s), "copy base");
+      mlxvs_b200::brute_force_knn(db, n, dq, nq, d, k, m, dids, ddist, s);
+    } else {
+      // chunk c's rows are searched (keys with global ids) as soon as they
+      // have landed, while the next chunks are still being copied; one merge
+      // of the chunks' lists gives the result (as for row shards on GPUs)
+      uint64_t* lists = static_cast<uint64_t*>(buf.alloc((size_t)chunks * count * 8));
+      cudaStream_t cs = thread_copy_stream();
+      std::vector<cudaEvent_t> ev(chunks + 1, nullptr);
+      for (auto& e : ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+      struct Events {
+        std::vector<cudaEvent_t>& e;
+        ~Events() {
+          for (auto x : e)
+            if (x) cudaEventDestroy(x);
+        }
+      } guard{ev};
+      ck(cudaEventRecord(ev[chunks], s), "event");  // the buffers exist
+      ck(cudaStreamWaitEvent(cs, ev[chunks], 0), "event");
+      auto rows = [&](int c) { return n * c / chunks; };
+      auto copy = [&](int c) {
+        const int64_t r0 = rows(c), r1 = rows(c + 1);
+        ck(cudaMemcpyAsync(db + r0 * d, base + r0 * d, (size_t)(r1 - r0) * d * sizeof(float),
+                           cudaMemcpyHostToDevice, cs), "copy base");
+        ck(cudaEventRecord(ev[c], cs), "event");
+      };
+      copy(0);
+      for (int c = 0; c < chunks; ++c) {
+        if (c + 1 < chunks) copy(c + 1);
+        ck(cudaStreamWaitEvent(s, ev[c], 0), "event");
+        const int64_t r0 = rows(c), r1 = rows(c + 1);
+        mlxvs_b200::knn_keys(db + r0 * d, r1 - r0, dq, nq, d, k, m, r0, lists + (size_t)c * count,
+                             s);
+      }
+      mlxvs_b200::merge_keys(lists, chunks, nq, k, static_cast<int>(m), dq, d, dids, ddist, s);
+    }
     ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
     if (distances)
       ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),

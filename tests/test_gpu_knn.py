@@ -285,3 +285,28 @@ def test_inexact_floats_near_ties():
     q = b[:300] + rng.standard_normal((300, 64)).astype(np.float32) * 1e-3
     ids, dist = mv.brute_force_knn(b, q, 10, "l2")
     check_float("l2", b, q, 10, ids, dist)
+
+
+@pytest.mark.parametrize("metric,k,integer", [("l2", 10, True), ("inner_product", 20, True),
+                                              ("cosine", 10, False)])
+def test_host_api_chunked_copy(metric, k, integer):
+    # host buffers of 2^18+ rows: the base is copied in chunks, each searched
+    # as it lands, and the chunks' lists merged; the results equal the
+    # device-pointer search (bit for bit on integer data)
+    import torch
+
+    if integer:
+        b, q = data.gaussian_mixture_int(300_001, 64, 64, seed=91, nq=500)
+    else:
+        b, q = data.lowrank_unit(300_001, 64, 16, seed=92, nq=500)
+    ids, dist = mv.brute_force_knn(b, q, k, metric)
+    dids, ddist = mv.brute_force_knn(torch.from_numpy(b).cuda(), torch.from_numpy(q).cuda(), k,
+                                     metric)
+    torch.cuda.synchronize()
+    if integer:
+        assert np.array_equal(ids, dids.cpu().numpy())
+        assert np.array_equal(dist, ddist.cpu().numpy())
+        oids, odist = O.brute_force_knn(b, q, k, metric)
+        assert np.array_equal(ids, oids) and np.array_equal(dist, odist)
+    else:
+        check_float(metric, b, q, k, ids, dist)
