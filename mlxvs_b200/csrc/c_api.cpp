@@ -118,6 +118,40 @@ int copy_chunks(int64_t n) {
   return (int)std::min<int64_t>(8, n >> 17);
 }
 
+// Copies host rows [n][row_elems] to dev_rows in `chunks` pieces on the copy
+// stream; search(c, dev_chunk, row0, rows) runs on s as soon as piece c has
+// landed, while later pieces are still being copied.
+template <class T, class Search>
+void copy_and_search(const T* host_rows, T* dev_rows, int64_t n, size_t row_elems, int chunks,
+                     cudaStream_t s, Search search) {
+  cudaStream_t cs = thread_copy_stream();
+  std::vector<cudaEvent_t> ev(chunks + 1, nullptr);
+  struct Events {
+    std::vector<cudaEvent_t>& e;
+    ~Events() {
+      for (auto x : e)
+        if (x) cudaEventDestroy(x);
+    }
+  } guard{ev};
+  for (auto& e : ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+  ck(cudaEventRecord(ev[chunks], s), "event");  // the device buffers exist
+  ck(cudaStreamWaitEvent(cs, ev[chunks], 0), "event");
+  auto row = [&](int c) { return n * c / chunks; };
+  auto copy = [&](int c) {
+    const int64_t r0 = row(c), r1 = row(c + 1);
+    ck(cudaMemcpyAsync(dev_rows + r0 * row_elems, host_rows + r0 * row_elems,
+                       (size_t)(r1 - r0) * row_elems * sizeof(T), cudaMemcpyHostToDevice, cs),
+       "copy rows");
+    ck(cudaEventRecord(ev[c], cs), "event");
+  };
+  copy(0);
+  for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) copy(c + 1);
+    ck(cudaStreamWaitEvent(s, ev[c], 0), "event");
+    search(c, dev_rows + row(c) * row_elems, row(c), row(c + 1) - row(c));
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -155,33 +189,11 @@ int mlxvs_brute_force_knn(const float* base, int64_t n, const float* queries, in
       // have landed, while the next chunks are still being copied; one merge
       // of the chunks' lists gives the result (as for row shards on GPUs)
       uint64_t* lists = static_cast<uint64_t*>(buf.alloc((size_t)chunks * count * 8));
-      cudaStream_t cs = thread_copy_stream();
-      std::vector<cudaEvent_t> ev(chunks + 1, nullptr);
-      for (auto& e : ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
-      struct Events {
-        std::vector<cudaEvent_t>& e;
-        ~Events() {
-          for (auto x : e)
-            if (x) cudaEventDestroy(x);
-        }
-      } guard{ev};
-      ck(cudaEventRecord(ev[chunks], s), "event");  // the buffers exist
-      ck(cudaStreamWaitEvent(cs, ev[chunks], 0), "event");
-      auto rows = [&](int c) { return n * c / chunks; };
-      auto copy = [&](int c) {
-        const int64_t r0 = rows(c), r1 = rows(c + 1);
-        ck(cudaMemcpyAsync(db + r0 * d, base + r0 * d, (size_t)(r1 - r0) * d * sizeof(float),
-                           cudaMemcpyHostToDevice, cs), "copy base");
-        ck(cudaEventRecord(ev[c], cs), "event");
-      };
-      copy(0);
-      for (int c = 0; c < chunks; ++c) {
-        if (c + 1 < chunks) copy(c + 1);
-        ck(cudaStreamWaitEvent(s, ev[c], 0), "event");
-        const int64_t r0 = rows(c), r1 = rows(c + 1);
-        mlxvs_b200::knn_keys(db + r0 * d, r1 - r0, dq, nq, d, k, m, r0, lists + (size_t)c * count,
-                             s);
-      }
+      copy_and_search(base, db, n, (size_t)d, chunks, s,
+                      [&](int c, const float* rows, int64_t r0, int64_t nr) {
+                        mlxvs_b200::knn_keys(rows, nr, dq, nq, d, k, m, r0,
+                                             lists + (size_t)c * count, s);
+                      });
       mlxvs_b200::merge_keys(lists, chunks, nq, k, static_cast<int>(m), dq, d, dids, ddist, s);
     }
     ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
@@ -351,9 +363,22 @@ int mlxvs_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries, in
     uint8_t* dq = static_cast<uint8_t*>(buf.alloc(qbytes));
     int32_t* dids = static_cast<int32_t*>(buf.alloc(count * sizeof(int32_t)));
     float* ddist = distances ? static_cast<float*>(buf.alloc(count * sizeof(float))) : nullptr;
-    if (rbytes) ck(cudaMemcpyAsync(dr, rows, rbytes, cudaMemcpyHostToDevice, s), "copy rows");
     ck(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, s), "copy queries");
-    mlxvs_b200::hamming_knn(dr, n, dq, nq, bytes, k, dids, ddist, s);
+    const int chunks = copy_chunks(n);
+    if (chunks == 1) {
+      if (rbytes) ck(cudaMemcpyAsync(dr, rows, rbytes, cudaMemcpyHostToDevice, s), "copy rows");
+      mlxvs_b200::hamming_knn(dr, n, dq, nq, bytes, k, dids, ddist, s);
+    } else {
+      // as mlxvs_brute_force_knn: chunks searched as they land, then merged
+      uint64_t* lists = static_cast<uint64_t*>(buf.alloc((size_t)chunks * count * 8));
+      copy_and_search(rows, dr, n, (size_t)bytes, chunks, s,
+                      [&](int c, const uint8_t* part, int64_t r0, int64_t nr) {
+                        mlxvs_b200::hamming_keys(part, nr, dq, nq, bytes, k, r0,
+                                                 lists + (size_t)c * count, s);
+                      });
+      mlxvs_b200::merge_keys(lists, chunks, nq, k, mlxvs_b200::KIND_HAMMING, nullptr, bytes, dids,
+                             ddist, s);
+    }
     ck(cudaMemcpyAsync(ids, dids, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s), "copy ids");
     if (distances)
       ck(cudaMemcpyAsync(distances, ddist, count * sizeof(float), cudaMemcpyDeviceToHost, s),

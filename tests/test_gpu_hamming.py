@@ -90,3 +90,18 @@ def test_device_and_sharded():
     assert np.array_equal(ids.cpu().numpy(), oids)
     assert np.array_equal(dist.cpu().numpy(), odist)
     mv.synchronize()
+
+
+def test_host_api_chunked_copy():
+    # 2^18+ codes from host memory: copied in chunks, each searched as it
+    # lands, the lists merged; bit-exact with the device entry and the oracle
+    import torch
+
+    rows, q = data.hamming_codes(300_001, 64, 1024, 0.1, seed=95, nq=300)
+    ids, dist = mv.hamming_knn(rows, q, 10)
+    dids, ddist = mv.hamming_knn(torch.from_numpy(rows).cuda(), torch.from_numpy(q).cuda(), 10)
+    torch.cuda.synchronize()
+    assert np.array_equal(ids, dids.cpu().numpy())
+    assert np.array_equal(dist, ddist.cpu().numpy())
+    oids, odist = O.hamming_knn(rows, q, 10)
+    assert np.array_equal(ids, oids) and np.array_equal(dist, odist)
