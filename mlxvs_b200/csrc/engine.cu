@@ -46,6 +46,7 @@ struct DeviceInfo {
   int sms = 0;
   int max_smem = 0;
   uint32_t* err = nullptr;  // error word of the kernels' bounded waits
+  size_t total_mem = 0;     // device memory in bytes
 };
 
 DeviceInfo& device_info() {
@@ -66,6 +67,10 @@ DeviceInfo& device_info() {
                                std::to_string(minor));
     CK(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&info.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    {
+      size_t free_b = 0;
+      CK(cudaMemGetInfo(&free_b, &info.total_mem));
+    }
     CK(cudaMalloc(&info.err, 16));
     CK(cudaMemset(info.err, 0, 16));
     // keep freed scratch in this process's pool between calls
@@ -765,7 +770,7 @@ void launch_hamming_v(const HammingParams& p, int QH, const DeviceInfo& dev, Scr
 // kind::i8 MMA pass of the fused kernel (s32 dots, exact), scores
 // -(bits - dot) / 2 = -distance, so the keys equal those of the popcount
 // kernel.  Returns false (nothing enqueued) when the unpacked rows would
-// take more than half of the free device memory.
+// take more than 40 % of the device's memory.
 bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq, int bytes,
                  int k, int64_t id_offset, uint64_t* out_keys, int32_t* ids, float* dist,
                  cudaStream_t s) {
@@ -775,9 +780,9 @@ bool hamming_mma(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t
   const int kchunks = d_pad / 128;
   const int64_t n_pad = round_up(n, GT_BN);
   const int64_t nq_pad = round_up(nq, 128);
-  size_t free_b = 0, total_b = 0;
-  CK(cudaMemGetInfo(&free_b, &total_b));
-  if ((double)(n_pad + nq_pad) * d_pad > 0.5 * (double)free_b) return false;
+  // (the device's total memory, read once: a query of the free memory on
+  // every call would cost a synchronization)
+  if ((double)(n_pad + nq_pad) * d_pad > 0.4 * (double)dev.total_mem) return false;
   const GemmShape sh = choose_shape(dev, 1, kchunks, k, 0, 1, 4);
   Scratch sc(s);
   int8_t* b8 = sc.alloc<int8_t>((size_t)n_pad * d_pad);
