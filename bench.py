@@ -45,6 +45,11 @@ WORKLOADS = {
     "knn-cos-1m-1536": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
                             metric="cosine", rank=64,
                             desc="config 2: 1M x 1536 fp32 unit rows, cosine, k=10"),
+    # config 2 at a fifth of the rows: the profiling case (a few GB on the
+    # device, still far larger than L2)
+    "knn-cos-200k-1536": dict(kind="knn-unit", n=200_000, nq=10_000, d=1536, k=10,
+                              metric="cosine", rank=64,
+                              desc="config 2 at 200k x 1536 unit rows, cosine, k=10"),
     # config 2 with float16 storage (the rows rounded to fp16, computed in
     # fp32 after the upcast, as the reference does with an f16 array)
     "knn-cos-1m-1536-f16": dict(kind="knn-unit", n=1_000_000, nq=10_000, d=1536, k=10,
@@ -74,8 +79,12 @@ METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pi
 # DRAM bytes per launch of the dominant kernel, from the committed ncu
 # summaries under profiles/ (None until captured for that workload).
 NCU_TRAFFIC_PER_LAUNCH = {
-    # profiles/knn_gemm_topk_config1.md: 386.8 MB read + 12.3 MB written
-    "knn-l2-1m-k10": 399.1e6,
+    # profiles/knn_gemm_topk_config1.md: 371.3 MB read + 11.8 MB written
+    "knn-l2-1m-k10": 383.1e6,
+    # profiles/knn_gemm_collect_config2_200k.md: the collecting pass
+    "knn-cos-200k-1536": 992.3e6,
+    # the same scaled by rows to config 2 (5x the base tiles)
+    "knn-cos-1m-1536": 4.962e9,
     # profiles/knn_gemm_topk_i8_hamming_1m.md: 3.32 GB at 1M codes
     "hamming-1m-1024b": 3.322e9,
     # the same, scaled by rows to 10M codes (10x the base tiles)
