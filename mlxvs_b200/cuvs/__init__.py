@@ -1,0 +1,6 @@
+"""A cuVS-style Python front end (``cuvs.distance``, ``cuvs.neighbors``) of
+the exact search, with cuVS's names, arguments, results and index files."""
+
+from mlxvs_b200.cuvs import distance, neighbors
+
+__all__ = ["distance", "neighbors"]
