@@ -438,8 +438,10 @@ def main():
     if is_hamming and kern_launches == 0:  # the tensor-core path ran
         kname = "hamming_mma"
         kern_ms, kern_launches = mv.profile_read(kname)
+    issued_ops = mv.profile_issued(kname)
     coll_ms, coll_launches = mv.profile_read("gemm_collect")
     if coll_launches > 0:
+        issued_ops += mv.profile_issued("gemm_collect")
         # k > 32: a sampled pass (lists of 1/4 of the base) and a collecting
         # pass over the whole base make up one search; both are counted
         kname = "gemm_topk (sampled pass) + gemm_collect"
@@ -537,12 +539,16 @@ def main():
             ach = ops / per_launch_s / 1e12
             peak = 2.0 * peaks["bf16_sustained"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
-                    "frac": ach / peak, "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
+                    "frac": ach / peak, "issued_frac": issued_ops / kern_launches
+                    / per_launch_s / 1e12 / peak,
+                    "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
                     "peak_source": f"2 x {peaks['source']} bf16 sustained",
                     "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"2*Q*N*bits = {ops:.3e} int8 ops "
                                               f"({w['nq'] * n_local * (bits // 32):.3e} "
-                                              f"32-bit popcounts' worth)"}
+                                              f"32-bit popcounts' worth)",
+                    "issued_per_launch": f"{issued_ops / kern_launches:.3e} int8 ops (padded "
+                                         f"query blocks x tiles x K)"}
         elif is_hamming:
             # integer work: 32-bit popcounts per launch; reported against the
             # HBM copy bandwidth is meaningless here (compute bound), so the
@@ -560,12 +566,17 @@ def main():
             ach = flops / per_launch_s / 1e12
             peak = peaks["bf16_sustained"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                    "frac": ach / peak, "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
+                    "frac": ach / peak, "issued_frac": issued_ops / kern_launches
+                    / per_launch_s / 1e12 / peak,
+                    "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
                     "peak_source": f"{peaks['source']} bf16 sustained (the kernel runs back to "
                                    f"back for the whole timed region)",
                     "frac_of_burst": ach / peaks["bf16"], "kernel": kname,
                     "kernel_ms": per_launch_s * 1e3,
-                    "algorithmic_per_launch": f"2*Q*N*D = {flops:.3e} FLOP"}
+                    "algorithmic_per_launch": f"2*Q*N*D = {flops:.3e} FLOP",
+                    "issued_per_launch": f"{issued_ops / kern_launches:.3e} FLOP (padded query "
+                                         f"blocks x tiles x (passes x padded D + 16 for "
+                                         f"|b|^2), sampled pass included)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -359,6 +359,15 @@ MLXVS_C_API int mlxvs_profile_enable(int32_t on);
  */
 MLXVS_C_API int mlxvs_profile_read(const char* kernel, double* total_ms, int64_t* launches);
 
+/**
+ * Benchmark support (not in the reference): the tensor-core operations
+ * (multiply-adds count 2) that the recorded launches of one kernel issued,
+ * or of all of them when kernel is NULL -- the MMA shape times the padded
+ * query blocks, tiles and K the kernel ran, against which the algorithmic
+ * 2*Q*N*D is the useful part.
+ */
+MLXVS_C_API int mlxvs_profile_issued(const char* kernel, double* tensor_ops);
+
 #ifdef __cplusplus
 }
 #endif

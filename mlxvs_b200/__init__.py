@@ -88,6 +88,7 @@ def _load():
         "mlxvs_profile_enable": [i32],
         "mlxvs_profile_read": [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                                ctypes.POINTER(ctypes.c_int64)],
+        "mlxvs_profile_issued": [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -549,3 +550,12 @@ def profile_read(kernel=None):
     name = kernel.encode() if kernel else None
     _check(_load().mlxvs_profile_read(name, ctypes.byref(ms), ctypes.byref(n)))
     return ms.value, n.value
+
+
+def profile_issued(kernel=None):
+    """Tensor-core operations (multiply-adds count 2) the recorded launches of
+    one kernel, or of all, issued: padded query blocks x tiles x issued K."""
+    ops = ctypes.c_double(0.0)
+    name = kernel.encode() if kernel else None
+    _check(_load().mlxvs_profile_issued(name, ctypes.byref(ops)))
+    return ops.value

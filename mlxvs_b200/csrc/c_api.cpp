@@ -461,6 +461,10 @@ int mlxvs_profile_read(const char* kernel, double* total_ms, int64_t* launches) 
   return guarded([&] { mlxvs_b200::profile_read(kernel, total_ms, launches); });
 }
 
+int mlxvs_profile_issued(const char* kernel, double* tensor_ops) {
+  return guarded([&] { mlxvs_b200::profile_issued(kernel, tensor_ops); });
+}
+
 int mlxvs_device_synchronize(void* stream) {
   return guarded([&] { mlxvs_b200::device_synchronize(static_cast<cudaStream_t>(stream)); });
 }

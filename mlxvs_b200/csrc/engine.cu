@@ -90,6 +90,7 @@ DeviceInfo& device_info() {
 struct ProfRecord {
   const char* name;
   cudaEvent_t start, stop;
+  double issued;  // tensor-core operations the launch issued (0: none)
 };
 std::mutex prof_mu;
 bool prof_on = false;
@@ -99,6 +100,7 @@ struct ProfScope {
   const char* name;
   cudaStream_t s;
   cudaEvent_t start = nullptr, stop = nullptr;
+  double issued = 0.0;
   ProfScope(const char* n, cudaStream_t st) : name(n), s(st) {
     bool on;
     {
@@ -114,7 +116,7 @@ struct ProfScope {
     if (!start) return;
     cudaEventRecord(stop, s);
     std::lock_guard<std::mutex> g(prof_mu);
-    prof_records.push_back({name, start, stop});
+    prof_records.push_back({name, start, stop, issued});
   }
 };
 
@@ -263,6 +265,12 @@ void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t s
   auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP, MODE>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   ProfScope prof(OP == 1 ? "hamming_mma" : (MODE == 1 ? "gemm_collect" : "gemm_topk"), s);
+  // every (query block, tile) pair runs 128 x 256 MMAs over the issued K:
+  // NPASS fp16 products per 64-column chunk plus the K=16 |b|^2 block, or
+  // 128 int8 columns per chunk
+  const double k_issued = OP == 1 ? 128.0 * p.kchunks
+                                  : (double)NPASS * GT_KCH * p.kchunks + 16.0 * p.extra;
+  prof.issued = 2.0 * 128.0 * GT_BN * k_issued * (double)p.qblocks * (double)p.tiles;
   kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo,
                                                               m.b_x, p);
   CK(cudaGetLastError());
@@ -1083,6 +1091,14 @@ void profile_enable(bool on) {
   }
   prof_records.clear();
   prof_on = on;
+}
+
+void profile_issued(const char* name, double* ops) {
+  std::lock_guard<std::mutex> g(prof_mu);
+  double total = 0.0;
+  for (auto& r : prof_records)
+    if (!name || std::strcmp(name, r.name) == 0) total += r.issued;
+  if (ops) *ops = total;
 }
 
 void profile_read(const char* name, double* total_ms, int64_t* launches) {

@@ -80,6 +80,7 @@ void profile_enable(bool on);
  * named `name` ("prep", "gemm_topk", "merge", "hamming_topk", "sumsq",
  * "fill"), or of all of them when name is null.  Waits for the events. */
 void profile_read(const char* name, double* total_ms, int64_t* launches);
+void profile_issued(const char* name, double* ops);
 
 /** Hamming k-NN with no device allocation: its scratch is a 16 MiB static
  * device array shared by all calls (they race if they overlap on the GPU).
