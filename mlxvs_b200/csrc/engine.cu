@@ -449,10 +449,12 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   pb.done = pa.done;
   pb.partial = pa.partial;  // not written in collect mode
   // some 10 k candidates per query are expected above the floor; room for
-  // about five times that, spread over the splits
-  pb.collect_cap = (int)round_up(std::max<int64_t>(256, (int64_t)48 * k / pb.splits), 64);
-  pb.collect = sc.alloc<uint64_t>((size_t)pb.splits * nq_pad * pb.collect_cap);
-  pb.collect_count = sc.alloc<int32_t>((size_t)pb.splits * nq_pad);
+  // about five times that, spread over the splits and their two column
+  // groups (one buffer each: `lists` per query)
+  const int lists = pb.splits * 2;
+  pb.collect_cap = (int)round_up(std::max<int64_t>(128, (int64_t)24 * k / pb.splits), 64);
+  pb.collect = sc.alloc<uint64_t>((size_t)lists * nq_pad * pb.collect_cap);
+  pb.collect_count = sc.alloc<int32_t>((size_t)lists * nq_pad);
   {
     const GemmSmem lay = gemm_smem(128, npa, 2, kchunks, sb.stages, sb.a_stream, 8, fold, 8, nbm);
     launch_shape(maps, pb, 128, 2, 8, exact, nbm, 1, lay.total + 1024u,
@@ -463,11 +465,11 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   if (rescore) {
     rescore->cand = pb.collect;
     rescore->count = pb.collect_count;
-    rescore->splits = pb.splits;
+    rescore->splits = lists;
     rescore->nq = nq;
     rescore->nq_pad = nq_pad;
     rescore->cap = pb.collect_cap;
-    const int64_t pairs = (int64_t)pb.splits * nq;
+    const int64_t pairs = (int64_t)lists * nq;
     ProfScope prof("rescore", s);
     rescore_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(*rescore);
     CK(cudaGetLastError());
@@ -480,7 +482,7 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   {
     ProfScope prof("select_keys", s);
     select_keys_kernel<<<(unsigned)nq, TOPK_THREADS, 0, s>>>(
-        pb.collect, pb.collect_count, pb.splits, nq_pad, pb.collect_cap, nq, k, best, overflow);
+        pb.collect, pb.collect_count, lists, nq_pad, pb.collect_cap, nq, k, best, overflow);
     CK(cudaGetLastError());
   }
   int32_t h_overflow = 0;

@@ -69,10 +69,11 @@ struct KnnGemmParams {
   // the shared floors of split s are gfloor + s * gfloor_split_stride (0:
   // one floor per query for all units)
   int64_t gfloor_split_stride;
-  // MODE 1 (collect): every candidate above the query's fixed floor goes to
-  // collect[(split * nq_pad + q) * collect_cap + i]; collect_count[split *
-  // nq_pad + q] receives how many there were (more than collect_cap means
-  // some were dropped and the caller must search another way)
+  // MODE 1 (collect): every candidate above the query's fixed floor that
+  // column group c of the unit sees goes to collect[((split * CG + c) *
+  // nq_pad + q) * collect_cap + i]; collect_count[(split * CG + c) * nq_pad +
+  // q] receives how many there were (more than collect_cap means some were
+  // dropped and the caller must search another way)
   uint64_t* collect;
   int32_t* collect_count;
   int32_t collect_cap;
@@ -163,8 +164,8 @@ __device__ __forceinline__ void heap_replace_root(uint64_t* heap, int k, uint64_
 }
 
 struct EpiState {
-  uint64_t* cbuf;  // MODE 1: this query's candidate buffer of this unit
-  int* ccnt;       // MODE 1: its count (shared memory)
+  uint64_t* cbuf;  // MODE 1: this (query, column group)'s buffer of this unit
+  int ccount;      // MODE 1: candidates offered to it so far
   uint32_t self_id;  // the query's own row id (all_neighbors), else 0xFFFFFFFF
   uint64_t floor;  // no candidate at or below this key can be in the result
   uint64_t gfl;    // the shared floor as last read or raised by this thread
@@ -317,8 +318,8 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const 
           if constexpr (MODE == 1) {
             // rows past nq (the last block's padding) have no buffer
             if (st.cbuf != nullptr && x > st.floor && id != st.self_id) {
-              const int at = atomicAdd(st.ccnt, 1);
-              if (at < p.collect_cap) st.cbuf[at] = x;
+              if (st.ccount < p.collect_cap) st.cbuf[st.ccount] = x;
+              ++st.ccount;
             }
             continue;
           }
@@ -393,8 +394,6 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < CG * QB; i += blockDim.x) fl_all[i] = 0ull;
-  if (MODE == 1)  // the per-query candidate counters live where the lists meet
-    for (int i = threadIdx.x; i < QB; i += blockDim.x) reinterpret_cast<int*>(heap_all)[i] = 0;
   if (warp == L::MMA) {
     tmem_alloc(tmem_slot, 2 * GT_BN);
     tmem_relinquish();
@@ -634,9 +633,9 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       st.self_id = (p.self_base >= 0 && q_ok) ? (uint32_t)(p.self_base + q) : 0xFFFFFFFFu;
       unsigned long long* gfl_q = p.gfloor + split * p.gfloor_split_stride + q;
       st.cbuf = (MODE == 1 && q_ok)
-                    ? p.collect + ((size_t)split * p.nq_pad + q) * (size_t)p.collect_cap
+                    ? p.collect + (((size_t)split * CG + ch) * p.nq_pad + q) * (size_t)p.collect_cap
                     : nullptr;
-      st.ccnt = reinterpret_cast<int*>(heap_all) + (row_on ? row : 0);
+      st.ccount = 0;
       st.gfl = q_ok ? *reinterpret_cast<volatile unsigned long long*>(gfl_q) : 0ull;
       if (inherited > st.gfl) st.gfl = inherited;
       st.floor = st.gfl;
@@ -761,14 +760,8 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
       }
       if (!ok) break;
       if constexpr (MODE == 1) {
-        // both column groups have appended: the count goes out and the
-        // counter is cleared before either group starts its next unit
-        if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
-        if (ch == 0 && row_on) {
-          if (q_ok) p.collect_count[(size_t)split * p.nq_pad + q] = *st.ccnt;
-          *st.ccnt = 0;
-        }
-        if (CG == 2) asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory");
+        // each column group's count of its own buffer
+        if (q_ok) p.collect_count[((size_t)split * CG + ch) * p.nq_pad + q] = st.ccount;
         continue;
       }
       if (CG == 2) {

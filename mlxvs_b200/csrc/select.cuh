@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   constexpr int WARPS = TOPK_THREADS / 32;
   __shared__ uint32_t hist[WARPS][256];
   __shared__ uint32_t suffix[256];
-  __shared__ uint32_t offs[65];
+  __shared__ uint32_t offs[129];
   __shared__ unsigned long long s_prefix;
   __shared__ uint32_t s_need, s_done;
   __shared__ uint32_t taken_above, taken_equal;
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   const int warp = lid >> 5;
   const int64_t q = blockIdx.x;
   if (q >= nq) return;
-  // prefix offsets of the splits' candidate runs (splits <= 64)
+  // prefix offsets of the buffers' candidate runs (splits <= 128)
   if (lid == 0) {
     uint32_t acc = 0;
     bool over = false;
@@ -314,9 +314,13 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   const uint32_t total = offs[splits];
   const uint32_t keff = (uint32_t)k < total ? (uint32_t)k : total;
   auto cand_at = [&](uint32_t i) -> uint64_t {
-    int sp = 0;
-    while (offs[sp + 1] <= i) ++sp;
-    return cand[((size_t)sp * nq_pad + q) * cap + (i - offs[sp])];
+    // the last buffer whose run starts at or before i (runs may be empty)
+    int lo = 0, hi = splits - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (offs[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    return cand[((size_t)lo * nq_pad + q) * cap + (i - offs[lo])];
   };
   uint64_t prefix = 0, mask = 0;
   uint32_t need = keff;
