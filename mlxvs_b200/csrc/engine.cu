@@ -350,18 +350,37 @@ void launch_shape(const GemmMaps& maps, const KnnGemmParams& p, int qb, int cg, 
 constexpr int LK_KG = 8;
 constexpr int LK_SAMPLE_DIV = 4;
 constexpr int LK_MIN_TILES = 16;
+// Listed-sample floors (exact operands, k >= LK_LISTED_MIN_K): the best
+// LK_KP of every LK_LISTED_C * k / LK_KP-th tile, so that some LK_LISTED_C * k
+// rows of the base clear the floor; at least LK_LISTED_MIN_TILES such tiles.
+// On rows in random order the number that clears it is about stride times
+// a Gamma(LK_KP) variable, whose mean is LK_LISTED_C * k; it falls below k,
+// a quarter of that, with probability about 1e-10 per query (the select
+// step then flags the query and the heap search runs instead).
+// Measured on config 1 against the grouped floors: k = 64 -3 %, 100 -14 %,
+// 128 -21 %, 256 -32 % per search; k = 48 +7 %, so not below 64.
+constexpr int LK_KP = 32;
+constexpr int LK_LISTED_C = 4;
+constexpr int LK_LISTED_MIN_K = 64;
+constexpr int LK_LISTED_MIN_TILES = 64;
 
 // Exact search for k > 16 in three steps instead of one pass with long
 // per-query lists (measured faster from k = 17 on):
-//   A. over G = ceil(k / LK_KG) disjoint strided samples of the base, the
-//      exact best ceil(k / G) of each (register lists, units that do not
-//      share lists or floors across samples); the smallest of the G worst
-//      keys has G * ceil(k / G) >= k rows at or above it: a floor;
+//   A. a floor per query, one of two ways:
+//      listed (exact operands, k >= LK_LISTED_MIN_K): the exact best LK_KP
+//      of a strided sample of the tiles, by the list kernel itself (shared
+//      floors, inherited lists); its worst key, which about LK_LISTED_C * k
+//      rows clear;
+//      grouped (otherwise): over G = ceil(k / LK_KG) disjoint strided
+//      samples, the exact best ceil(k / G) of each (units that do not share
+//      lists or floors across samples); the smallest of the G worst keys has
+//      G * ceil(k / G) >= k rows at or above it;
 //   B. over the whole base, every candidate above that floor is kept
-//      (collect mode, per (split, query) buffers);
+//      (collect mode, per (split, query, column group) buffers);
 //   C. the best k of the kept candidates, then keys -> ids / distances.
 // Returns false, having enqueued only harmless work, when a query kept more
-// candidates than its buffers hold (the caller then searches with heaps).
+// candidates than its buffers hold, or (listed floors) fewer than k: the
+// caller then searches with heaps.
 bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exact, int nbm,
                     int npa, int kchunks, bool fold, const __half* q_hi, const __half* q_lo,
                     int64_t nq_pad, int d_pad, int mi, const float* qq, uint64_t* out_keys,
@@ -390,48 +409,94 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   }
   const int kg = (k + G - 1) / G;
   const int sample_tiles = std::max(LK_MIN_TILES * G, tiles / LK_SAMPLE_DIV);
-  if ((k <= 16 && rescore == nullptr) || sample_tiles > tiles || nq_pad % 128 != 0) return false;
+  if ((k <= 16 && rescore == nullptr) || nq_pad % 128 != 0) return false;
   const int want = exact ? 4 : 2;
-  const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
   const GemmShape sb = choose_shape(dev, npa, kchunks, 8, fold ? 1 : 0, nbm, want);
-  if (sa.qb != 128 || sa.cg != 2 || sa.kr == 0 || sb.qb != 128 || sb.cg != 2 || sb.kr != 8)
+  if (sb.qb != 128 || sb.cg != 2 || sb.kr != 8) return false;
+  // the listed sample: floors shared by the sample's splits and lists
+  // inherited across them, so only the first wave of units starts cold
+  const int lstride = std::max(2, LK_LISTED_C * k / LK_KP);
+  const int ltiles = tiles / lstride;
+  const GemmShape sl = choose_shape(dev, npa, kchunks, LK_KP, fold ? 1 : 0, nbm, want);
+  const bool listed = rescore == nullptr && k >= LK_LISTED_MIN_K &&
+                      ltiles >= LK_LISTED_MIN_TILES && sl.qb == 128 && sl.cg == 2 &&
+                      sl.kr == LK_KP;
+  const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
+  if (!listed && (sample_tiles > tiles || sa.qb != 128 || sa.cg != 2 || sa.kr == 0))
     return false;
   const int64_t nq = p_in.nq;
   const int qblocks = (int)((nq + 127) / 128);
   GemmMaps maps = maps_in;
   maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, 128);
   maps.a_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, 128);
-
-  // A: per-sample exact lists
-  KnnGemmParams pa = p_in;
-  pa.qblocks = qblocks;
-  pa.tiles = sample_tiles;
-  pa.splits = G;
-  pa.units = qblocks * G;
-  pa.k = kg;
-  pa.stages = sa.stages;
-  pa.a_stream = sa.a_stream;
-  pa.tile_stride = tiles / sample_tiles;
-  pa.no_inherit = 1;
-  pa.gfloor_split_stride = nq_pad;
-  pa.gfloor = sc.alloc<unsigned long long>((size_t)G * nq_pad);
-  CK(cudaMemsetAsync(pa.gfloor, 0, (size_t)G * nq_pad * 8, s));
-  pa.partial = sc.alloc<uint64_t>((size_t)G * nq_pad * kg);
-  pa.done = sc.alloc<int>((size_t)qblocks);
-  CK(cudaMemsetAsync(pa.done, 0, (size_t)qblocks * 4, s));
-  {
-    const GemmSmem lay = gemm_smem(128, npa, 2, kchunks, sa.stages, sa.a_stream, kg, fold, sa.kr,
-                                   nbm);
-    launch_shape(maps, pa, 128, 2, sa.kr, exact, nbm, 0, lay.total + 1024u,
-                 std::min(pa.units, dev.sms), s);
-  }
   unsigned long long* floor = sc.alloc<unsigned long long>((size_t)nq_pad);
-  sample_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(pa.partial, G, nq_pad, kg,
-                                                                         nq, floor);
-  CK(cudaGetLastError());
-  if (rescore) {
-    margin_floor_kernel<<<(unsigned)((nq + 255) / 256), 256, 0, s>>>(floor, nq, eps);
+  int* done = sc.alloc<int>((size_t)qblocks);
+  CK(cudaMemsetAsync(done, 0, (size_t)qblocks * 4, s));
+  uint64_t* partial_a = nullptr;
+  int32_t k_min = 0;  // candidates every query must keep (listed floors only)
+
+  if (listed) {
+    // A': the exact best LK_KP of every lstride-th tile; its worst key is a
+    // floor that some LK_KP * lstride rows clear on average but, for k >
+    // LK_KP, not surely k of them: step C checks that
+    KnnGemmParams pa = p_in;
+    pa.qblocks = qblocks;
+    pa.tiles = ltiles;
+    pa.tile_stride = lstride;
+    pa.splits = choose_splits(qblocks, ltiles, dev.sms, 3.0, 64);
+    pa.units = qblocks * pa.splits;
+    pa.k = LK_KP;
+    pa.stages = sl.stages;
+    pa.a_stream = sl.a_stream;
+    pa.no_inherit = 0;
+    pa.gfloor_split_stride = 0;
+    pa.gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
+    CK(cudaMemsetAsync(pa.gfloor, 0, (size_t)nq_pad * 8, s));
+    pa.partial = sc.alloc<uint64_t>((size_t)pa.splits * nq_pad * LK_KP);
+    pa.done = done;
+    const GemmSmem lay =
+        gemm_smem(128, npa, 2, kchunks, sl.stages, sl.a_stream, LK_KP, fold, LK_KP, nbm);
+    launch_shape(maps, pa, 128, 2, LK_KP, exact, nbm, 0, lay.total + 1024u,
+                 std::min(pa.units, dev.sms), s);
+    uint64_t* top = sc.alloc<uint64_t>((size_t)nq * LK_KP);
+    launch_merge(pa.partial, pa.splits, nq_pad, nq, LK_KP, mi, nullptr, top, nullptr, nullptr, s);
+    list_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(top, LK_KP, nq, nq_pad,
+                                                                       floor);
     CK(cudaGetLastError());
+    partial_a = pa.partial;
+    const int64_t avail = p_in.n_valid - (p_in.self_base >= 0 ? 1 : 0);
+    k_min = (int32_t)std::min<int64_t>(k, avail);
+  } else {
+    // A: per-sample exact lists
+    KnnGemmParams pa = p_in;
+    pa.qblocks = qblocks;
+    pa.tiles = sample_tiles;
+    pa.splits = G;
+    pa.units = qblocks * G;
+    pa.k = kg;
+    pa.stages = sa.stages;
+    pa.a_stream = sa.a_stream;
+    pa.tile_stride = tiles / sample_tiles;
+    pa.no_inherit = 1;
+    pa.gfloor_split_stride = nq_pad;
+    pa.gfloor = sc.alloc<unsigned long long>((size_t)G * nq_pad);
+    CK(cudaMemsetAsync(pa.gfloor, 0, (size_t)G * nq_pad * 8, s));
+    pa.partial = sc.alloc<uint64_t>((size_t)G * nq_pad * kg);
+    pa.done = done;
+    {
+      const GemmSmem lay = gemm_smem(128, npa, 2, kchunks, sa.stages, sa.a_stream, kg, fold, sa.kr,
+                                     nbm);
+      launch_shape(maps, pa, 128, 2, sa.kr, exact, nbm, 0, lay.total + 1024u,
+                   std::min(pa.units, dev.sms), s);
+    }
+    sample_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(pa.partial, G, nq_pad, kg,
+                                                                           nq, floor);
+    CK(cudaGetLastError());
+    if (rescore) {
+      margin_floor_kernel<<<(unsigned)((nq + 255) / 256), 256, 0, s>>>(floor, nq, eps);
+      CK(cudaGetLastError());
+    }
+    partial_a = pa.partial;
   }
 
   // B: every candidate above the floor
@@ -446,8 +511,8 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   pb.no_inherit = 1;
   pb.gfloor = floor;
   pb.gfloor_split_stride = 0;
-  pb.done = pa.done;
-  pb.partial = pa.partial;  // not written in collect mode
+  pb.done = done;
+  pb.partial = partial_a;  // not written in collect mode
   // some 10 k candidates per query are expected above the floor; room for
   // about five times that, spread over the splits and their two column
   // groups (one buffer each: `lists` per query)
@@ -482,7 +547,8 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   {
     ProfScope prof("select_keys", s);
     select_keys_kernel<<<(unsigned)nq, TOPK_THREADS, 0, s>>>(
-        pb.collect, pb.collect_count, lists, nq_pad, pb.collect_cap, nq, k, best, overflow);
+        pb.collect, pb.collect_count, lists, nq_pad, pb.collect_cap, nq, k, k_min, best,
+        overflow);
     CK(cudaGetLastError());
   }
   int32_t h_overflow = 0;

@@ -199,6 +199,17 @@ __global__ void sample_floor_kernel(const uint64_t* __restrict__ lists, int32_t 
   floor[q] = f == 0 ? 0ull : (unsigned long long)(f - 1);
 }
 
+// The floor of the listed-sample search: each query's kp-th best key of the
+// sample (merged lists, best first), less one; 0 (no floor) when the sample
+// held fewer than kp rows or for padding rows.
+__global__ void list_floor_kernel(const uint64_t* __restrict__ top, int32_t kp, int64_t nq,
+                                  int64_t nq_pad, unsigned long long* __restrict__ floor) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq_pad) return;
+  const uint64_t f = q < nq ? top[(size_t)q * kp + kp - 1] : 0ull;
+  floor[q] = f == 0 ? 0ull : (unsigned long long)(f - 1);
+}
+
 // One fp16 pass on inexact operands: lowers each query's floor (a key F - 1,
 // from sample_floor_kernel) by 2 eps, eps bounding |fp16 score - exact
 // score| in the same units: every row of the exact best k then scores at
@@ -279,12 +290,14 @@ __global__ void rescore_kernel(RescoreParams p) {
 // Large k, last step: the best k keys of the candidates the collecting pass
 // kept for each query (splits x cap keys, count[s * nq_pad + q] of them per
 // split), best first, 0-padded; a count above cap (candidates dropped) sets
-// *overflow.  One block per query: the radix select of topk_rows_kernel on
+// bit 0 of *overflow, fewer than k_min candidates in all (a floor that too
+// few rows cleared) bit 1.  One block per query: the radix select of topk_rows_kernel on
 // the keys themselves, then a bitonic sort by key.
 __global__ void __launch_bounds__(TOPK_THREADS)
     select_keys_kernel(const uint64_t* __restrict__ cand, const int32_t* __restrict__ count,
                        int32_t splits, int64_t nq_pad, int32_t cap, int64_t nq, int32_t k,
-                       uint64_t* __restrict__ out, int32_t* __restrict__ overflow) {
+                       int32_t k_min, uint64_t* __restrict__ out,
+                       int32_t* __restrict__ overflow) {
   constexpr int WARPS = TOPK_THREADS / 32;
   __shared__ uint32_t hist[WARPS][256];
   __shared__ uint32_t suffix[256];
@@ -309,6 +322,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     }
     offs[splits] = acc;
     if (over) atomicOr(overflow, 1);
+    if (acc < (uint32_t)k_min) atomicOr(overflow, 2);
   }
   __syncthreads();
   const uint32_t total = offs[splits];

@@ -251,6 +251,48 @@ def test_large_k_sampled_floor_path(metric, k):
     assert np.array_equal(dist, odist)
 
 
+@pytest.mark.parametrize("n,d,k", [(140_000, 32, 64), (250_000, 32, 100), (600_000, 16, 256)])
+def test_large_k_listed_floor_path(n, d, k):
+    # k >= 64 on a base of 64+ sampled tiles: the floor is the list kernel's
+    # best 32 of every (4 k / 32)-th tile; integer data bit-exact
+    import torch
+
+    b, q = data.gaussian_mixture_int(n, d, 64, seed=73, nq=150)
+    # device tensors: one search over the whole base (the host entry would
+    # search a base this large in chunks)
+    tids, tdist = mv.brute_force_knn(torch.from_numpy(b).cuda(), torch.from_numpy(q).cuda(), k,
+                                     "l2")
+    ids, dist = tids.cpu().numpy(), tdist.cpu().numpy()
+    oids, odist = O.brute_force_knn(b, q, k, "l2")
+    assert np.array_equal(ids, oids)
+    assert np.array_equal(dist, odist)
+
+
+def test_large_k_listed_floor_underflow_falls_back():
+    # every near row sits in the sampled tiles (every 12th tile for k = 100),
+    # so only the sample's best 32 clear its floor: the select step flags
+    # the queries and the heap search gives the result
+    n, d, k = 200_000, 16, 100
+    rng = np.random.default_rng(74)
+    b = np.full((n, d), 50.0, np.float32)
+    tiles = (n + 255) // 256
+    for t in range(0, tiles, 12):
+        lo, hi = t * 256, min(n, t * 256 + 256)
+        b[lo:hi] = rng.integers(0, 4, (hi - lo, d)).astype(np.float32)
+    q = np.zeros((8, d), np.float32)
+    mv.profile_enable(True)
+    try:
+        ids, dist = mv.brute_force_knn(b, q, k, "l2")
+        _, gemm_launches = mv.profile_read("gemm_topk")
+        _, collect_launches = mv.profile_read("gemm_collect")
+    finally:
+        mv.profile_enable(False)
+    assert collect_launches == 1 and gemm_launches == 2  # sample pass, then the heaps
+    oids, odist = O.brute_force_knn(b, q, k, "l2")
+    assert np.array_equal(ids, oids)
+    assert np.array_equal(dist, odist)
+
+
 def test_large_k_overflow_falls_back():
     # identical rows: every row ties the floor, the kept candidates overflow
     # their buffers and the search falls back to per-query heaps; the result
