@@ -350,27 +350,30 @@ void launch_shape(const GemmMaps& maps, const KnnGemmParams& p, int qb, int cg, 
 constexpr int LK_KG = 8;
 constexpr int LK_SAMPLE_DIV = 4;
 constexpr int LK_MIN_TILES = 16;
-// Listed-sample floors (exact operands, k >= LK_LISTED_MIN_K): the best
-// LK_KP of every LK_LISTED_C * k / LK_KP-th tile, so that some LK_LISTED_C * k
-// rows of the base clear the floor; at least LK_LISTED_MIN_TILES such tiles.
-// On rows in random order the number that clears it is about stride times
-// a Gamma(LK_KP) variable, whose mean is LK_LISTED_C * k; it falls below k,
-// a quarter of that, with probability about 1e-10 per query (the select
-// step then flags the query and the heap search runs instead).
-// Measured on config 1 against the grouped floors: k = 64 -3 %, 100 -14 %,
-// 128 -21 %, 256 -32 % per search; k = 48 +7 %, so not below 64.
-constexpr int LK_KP = 32;
-constexpr int LK_LISTED_C = 4;
-constexpr int LK_LISTED_MIN_K = 64;
+// Listed-sample floors (exact operands, k >= LK_LISTED_MIN_K): the best kp
+// of every (c * k / kp)-th tile, so that some c * k rows of the base clear
+// the floor, with (kp, c) = (16, 6) when that sample keeps at least
+// LK_LISTED_MIN_TILES tiles, else (32, 4).  On rows in random order the
+// number that clears it is about the stride times a Gamma(kp) variable,
+// whose mean is c * k; it falls below k with probability about 2e-8 per
+// query for (16, 6) and 1e-10 for (32, 4) (the select step then flags the
+// query and the heap search runs instead).  Measured on config 1 against
+// the grouped floors: k = 17 -3 %, 24 -10 %, 32 -13 %, 64 -23 %, 100 -26 %,
+// 128 -27 %, 256 -32 % per search.
+struct ListedSample {
+  int kp, c;
+};
+constexpr ListedSample LK_LISTED[2] = {{16, 6}, {32, 4}};
+constexpr int LK_LISTED_MIN_K = 17;
 constexpr int LK_LISTED_MIN_TILES = 64;
 
 // Exact search for k > 16 in three steps instead of one pass with long
 // per-query lists (measured faster from k = 17 on):
 //   A. a floor per query, one of two ways:
-//      listed (exact operands, k >= LK_LISTED_MIN_K): the exact best LK_KP
-//      of a strided sample of the tiles, by the list kernel itself (shared
-//      floors, inherited lists); its worst key, which about LK_LISTED_C * k
-//      rows clear;
+//      listed (exact operands, k >= LK_LISTED_MIN_K): the exact best kp of
+//      a strided sample of the tiles, by the list kernel itself (shared
+//      floors, inherited lists); its worst key, which about c * k rows
+//      clear;
 //      grouped (otherwise): over G = ceil(k / LK_KG) disjoint strided
 //      samples, the exact best ceil(k / G) of each (units that do not share
 //      lists or floors across samples); the smallest of the G worst keys has
@@ -415,12 +418,17 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   if (sb.qb != 128 || sb.cg != 2 || sb.kr != 8) return false;
   // the listed sample: floors shared by the sample's splits and lists
   // inherited across them, so only the first wave of units starts cold
-  const int lstride = std::max(2, LK_LISTED_C * k / LK_KP);
-  const int ltiles = tiles / lstride;
-  const GemmShape sl = choose_shape(dev, npa, kchunks, LK_KP, fold ? 1 : 0, nbm, want);
+  int kp = 0, lstride = 0, ltiles = 0;
+  for (const ListedSample& ls : LK_LISTED) {
+    kp = ls.kp;
+    lstride = std::max(2, ls.c * k / kp);
+    ltiles = tiles / lstride;
+    if (ltiles >= LK_LISTED_MIN_TILES) break;
+  }
+  const GemmShape sl = choose_shape(dev, npa, kchunks, kp, fold ? 1 : 0, nbm, want);
   const bool listed = rescore == nullptr && k >= LK_LISTED_MIN_K &&
                       ltiles >= LK_LISTED_MIN_TILES && sl.qb == 128 && sl.cg == 2 &&
-                      sl.kr == LK_KP;
+                      sl.kr == kp;
   const GemmShape sa = choose_shape(dev, npa, kchunks, kg, fold ? 1 : 0, nbm, want);
   if (!listed && (sample_tiles > tiles || sa.qb != 128 || sa.cg != 2 || sa.kr == 0))
     return false;
@@ -436,31 +444,31 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   int32_t k_min = 0;  // candidates every query must keep (listed floors only)
 
   if (listed) {
-    // A': the exact best LK_KP of every lstride-th tile; its worst key is a
-    // floor that some LK_KP * lstride rows clear on average but, for k >
-    // LK_KP, not surely k of them: step C checks that
+    // A': the exact best kp of every lstride-th tile; its worst key is a
+    // floor that some kp * lstride rows clear on average but, for k > kp,
+    // not surely k of them: step C checks that
     KnnGemmParams pa = p_in;
     pa.qblocks = qblocks;
     pa.tiles = ltiles;
     pa.tile_stride = lstride;
     pa.splits = choose_splits(qblocks, ltiles, dev.sms, 3.0, 64);
     pa.units = qblocks * pa.splits;
-    pa.k = LK_KP;
+    pa.k = kp;
     pa.stages = sl.stages;
     pa.a_stream = sl.a_stream;
     pa.no_inherit = 0;
     pa.gfloor_split_stride = 0;
     pa.gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
     CK(cudaMemsetAsync(pa.gfloor, 0, (size_t)nq_pad * 8, s));
-    pa.partial = sc.alloc<uint64_t>((size_t)pa.splits * nq_pad * LK_KP);
+    pa.partial = sc.alloc<uint64_t>((size_t)pa.splits * nq_pad * kp);
     pa.done = done;
     const GemmSmem lay =
-        gemm_smem(128, npa, 2, kchunks, sl.stages, sl.a_stream, LK_KP, fold, LK_KP, nbm);
-    launch_shape(maps, pa, 128, 2, LK_KP, exact, nbm, 0, lay.total + 1024u,
+        gemm_smem(128, npa, 2, kchunks, sl.stages, sl.a_stream, kp, fold, kp, nbm);
+    launch_shape(maps, pa, 128, 2, kp, exact, nbm, 0, lay.total + 1024u,
                  std::min(pa.units, dev.sms), s);
-    uint64_t* top = sc.alloc<uint64_t>((size_t)nq * LK_KP);
-    launch_merge(pa.partial, pa.splits, nq_pad, nq, LK_KP, mi, nullptr, top, nullptr, nullptr, s);
-    list_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(top, LK_KP, nq, nq_pad,
+    uint64_t* top = sc.alloc<uint64_t>((size_t)nq * kp);
+    launch_merge(pa.partial, pa.splits, nq_pad, nq, kp, mi, nullptr, top, nullptr, nullptr, s);
+    list_floor_kernel<<<(unsigned)((nq_pad + 255) / 256), 256, 0, s>>>(top, kp, nq, nq_pad,
                                                                        floor);
     CK(cudaGetLastError());
     partial_a = pa.partial;

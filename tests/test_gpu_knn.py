@@ -251,10 +251,13 @@ def test_large_k_sampled_floor_path(metric, k):
     assert np.array_equal(dist, odist)
 
 
-@pytest.mark.parametrize("n,d,k", [(140_000, 32, 64), (250_000, 32, 100), (600_000, 16, 256)])
+@pytest.mark.parametrize("n,d,k", [(140_000, 32, 64), (250_000, 32, 100), (600_000, 16, 256),
+                                   (300_000, 32, 17), (700_000, 16, 100)])
 def test_large_k_listed_floor_path(n, d, k):
-    # k >= 64 on a base of 64+ sampled tiles: the floor is the list kernel's
-    # best 32 of every (4 k / 32)-th tile; integer data bit-exact
+    # k > 16 on a base of 64+ sampled tiles: the floor is the list kernel's
+    # best 16 of every (6 k / 16)-th tile (the last two cases) or, where
+    # that sample is too small, its best 32 of every (4 k / 32)-th tile;
+    # integer data bit-exact
     import torch
 
     b, q = data.gaussian_mixture_int(n, d, 64, seed=73, nq=150)
@@ -268,21 +271,27 @@ def test_large_k_listed_floor_path(n, d, k):
     assert np.array_equal(dist, odist)
 
 
-def test_large_k_listed_floor_underflow_falls_back():
-    # every near row sits in the sampled tiles (every 12th tile for k = 100),
-    # so only the sample's best 32 clear its floor: the select step flags
-    # the queries and the heap search gives the result
-    n, d, k = 200_000, 16, 100
+@pytest.mark.parametrize("n,stride", [(200_000, 12), (610_000, 37)])
+def test_large_k_listed_floor_underflow_falls_back(n, stride):
+    # every near row sits in the sampled tiles (for k = 100 every 12th tile
+    # with 32-key sample lists, every 37th with 16-key ones), so only the
+    # sample's best kp clear its floor: the select step flags the queries
+    # and the heap search gives the result
+    import torch
+
+    d, k = 16, 100
     rng = np.random.default_rng(74)
     b = np.full((n, d), 50.0, np.float32)
     tiles = (n + 255) // 256
-    for t in range(0, tiles, 12):
+    for t in range(0, tiles, stride):
         lo, hi = t * 256, min(n, t * 256 + 256)
         b[lo:hi] = rng.integers(0, 4, (hi - lo, d)).astype(np.float32)
     q = np.zeros((8, d), np.float32)
     mv.profile_enable(True)
     try:
-        ids, dist = mv.brute_force_knn(b, q, k, "l2")
+        tids, tdist = mv.brute_force_knn(torch.from_numpy(b).cuda(), torch.from_numpy(q).cuda(),
+                                         k, "l2")
+        ids, dist = tids.cpu().numpy(), tdist.cpu().numpy()
         _, gemm_launches = mv.profile_read("gemm_topk")
         _, collect_launches = mv.profile_read("gemm_collect")
     finally:
