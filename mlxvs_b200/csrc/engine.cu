@@ -357,12 +357,28 @@ constexpr int LK_MIN_TILES = 16;
 // number that clears it is about the stride times a Gamma(kp) variable,
 // whose mean is c * k; it falls below k with probability about 2e-8 per
 // query for (16, 6) and 1e-10 for (32, 4) (the select step then flags the
-// query and the heap search runs instead).  Measured on config 1 against
+// query and the heap search runs instead); c grows with the number of
+// queries so that a search needs that fallback with probability < 1e-3.  Measured on config 1 against
 // the grouped floors: k = 17 -3 %, 24 -10 %, 32 -13 %, 64 -23 %, 100 -26 %,
 // 128 -27 %, 256 -32 % per search.
 struct ListedSample {
-  int kp, c;
+  int kp, c;  // sample list length, least collection factor
 };
+
+// The chance that fewer than k rows of a base in random order clear a
+// listed floor of kp keys taken at stride c k / kp: P(Gamma(kp) < kp / c),
+// i.e. P(Poisson(kp / c) >= kp).
+double listed_underflow(int kp, int c) {
+  const double lam = (double)kp / c;
+  double term = std::exp(-lam);
+  for (int i = 1; i <= kp; ++i) term *= lam / i;
+  double tail = 0.0;
+  for (int i = kp; i < kp + 64 && term > 0.0; ++i) {
+    tail += term;
+    term *= lam / (i + 1);
+  }
+  return tail;
+}
 constexpr ListedSample LK_LISTED[2] = {{16, 6}, {32, 4}};
 constexpr int LK_LISTED_MIN_K = 17;
 constexpr int LK_LISTED_MIN_TILES = 64;
@@ -421,7 +437,11 @@ bool large_k_search(const GemmMaps& maps_in, const KnnGemmParams& p_in, bool exa
   int kp = 0, lstride = 0, ltiles = 0;
   for (const ListedSample& ls : LK_LISTED) {
     kp = ls.kp;
-    lstride = std::max(2, ls.c * k / kp);
+    // the factor grows with the queries until the chance that any of them
+    // needs the fallback is under 1e-3 (config 3's 1M queries: 8 for kp 16)
+    int c = ls.c;
+    while (c < 16 && (double)p_in.nq * listed_underflow(kp, c) > 1e-3) ++c;
+    lstride = std::max(2, c * k / kp);
     ltiles = tiles / lstride;
     if (ltiles >= LK_LISTED_MIN_TILES) break;
   }
