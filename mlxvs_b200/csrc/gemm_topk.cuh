@@ -253,6 +253,58 @@ __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
   }
 }
 
+// The register lists' slow path for 16 scores v[0..15] of columns col0..:
+// every lane calls it (the votes are warp-wide); `mine` marks the lanes with
+// a score at or above their floor.  Each such lane marks those scores in a
+// 16-bit mask, the scores go through this warp's shared column (sv, stride
+// 32), and the warp loops only while some lane still has marked scores
+// (usually once or twice, not 16 times).
+template <int KR, int MODE>
+__device__ __forceinline__ void epi_slow_list16(const float* v, bool mine, int64_t col0,
+                                                const KnnGemmParams& p,
+                                                uint64_t (&key)[KR > 0 ? KR : 1], float* sv,
+                                                EpiState& st) {
+  if (!__any_sync(0xffffffffu, mine)) return;
+  uint32_t mask = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    sv[j * 32] = v[j];
+    mask |= (v[j] >= st.thr ? 1u : 0u) << j;
+  }
+  if (!mine) mask = 0;
+  if (col0 + 16 > p.n_valid) {
+    const int64_t valid = p.n_valid - col0;
+    mask &= valid <= 0 ? 0u : (valid >= 16 ? 0xFFFFu : ((1u << valid) - 1u));
+  }
+  __syncwarp();
+  const uint32_t id0 = (uint32_t)(p.id_offset + col0);
+  while (__any_sync(0xffffffffu, mask != 0)) {
+    if (mask) {
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1;
+      const float vj = sv[j * 32];
+      const uint32_t id = id0 + (uint32_t)j;
+      const uint64_t x = make_key(vj, id);
+      if constexpr (MODE == 1) {
+        // rows past nq (the last block's padding) have no buffer
+        if (st.cbuf != nullptr && x > st.floor && id != st.self_id) {
+          if (st.ccount < p.collect_cap) st.cbuf[st.ccount] = x;
+          ++st.ccount;
+        }
+        continue;
+      }
+      if constexpr (KR > 0) {
+        if (x > st.floor && id != st.self_id) {
+          list_insert<KR>(key, x);
+          if (key[0] > st.floor) st.floor = key[0];
+          st.thr = key_score(st.floor);
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // 16 scores (raw dots r[o..o+15] minus the per-row terms nbs[0..15]): reject
 // with one compare when their max is below the floor, else offer each.
 template <int HS, int NBM, int KR, int OP, int MODE, int RN>
@@ -289,49 +341,51 @@ __device__ __forceinline__ void epi_sub16(const uint32_t (&r)[RN], int o, const 
                           v[11], v[12], v[13], v[14], v[15], col0, p.n_valid,
                           (uint32_t)(p.id_offset + col0), heap, p.k, st);
   } else {
-    // warp-uniform slow path: each lane marks its scores at or above its
-    // floor in a 16-bit mask; the scores go through this warp's shared
-    // column (sv, stride 32), and the warp loops only while some lane still
-    // has marked scores (usually once or twice, not 16 times)
-    const bool mine = row_on && mx >= st.thr;
-    if (__any_sync(0xffffffffu, mine)) {
-      uint32_t mask = 0;
+    epi_slow_list16<KR, MODE>(v, row_on && mx >= st.thr, col0, p, key, sv, st);
+  }
+}
+
+// 32 scores (r[0..31] minus nbs[0..31]) for the register lists: two
+// 16-score maxima and one warp vote for both, so the common case (no lane
+// above its floor) pays one vote and branch per 32 scores.  Used where the
+// accumulator already is the score (NBM = 1; with the per-row terms the 32
+// live scores spill) and for lists (in collect mode, where the floor is
+// lower and votes succeed more often, it measured 1 % slower).  Config 1:
+// -1.2 % kernel time.
+template <int NBM, int KR, int OP, int MODE>
+__device__ __forceinline__ void epi_sub32(const uint32_t (&r)[32], const float* nbs,
+                                          int64_t col0, const KnnGemmParams& p, bool row_on,
+                                          uint64_t (&key)[KR], float* sv, EpiState& st) {
+  float v[32];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        sv[j * 32] = v[j];
-        mask |= (v[j] >= st.thr ? 1u : 0u) << j;
-      }
-      if (!mine) mask = 0;
-      if (col0 + 16 > p.n_valid) {
-        const int64_t valid = p.n_valid - col0;
-        mask &= valid <= 0 ? 0u : (valid >= 16 ? 0xFFFFu : ((1u << valid) - 1u));
-      }
-      __syncwarp();
-      const uint32_t id0 = (uint32_t)(p.id_offset + col0);
-      while (__any_sync(0xffffffffu, mask != 0)) {
-        if (mask) {
-          const int j = __ffs(mask) - 1;
-          mask &= mask - 1;
-          const float vj = sv[j * 32];
-          const uint32_t id = id0 + (uint32_t)j;
-          const uint64_t x = make_key(vj, id);
-          if constexpr (MODE == 1) {
-            // rows past nq (the last block's padding) have no buffer
-            if (st.cbuf != nullptr && x > st.floor && id != st.self_id) {
-              if (st.ccount < p.collect_cap) st.cbuf[st.ccount] = x;
-              ++st.ccount;
-            }
-            continue;
-          }
-          if (x > st.floor && id != st.self_id) {
-            list_insert<KR>(key, x);
-            if (key[0] > st.floor) st.floor = key[0];
-            st.thr = key_score(st.floor);
-          }
-        }
-      }
-      __syncwarp();
+  for (int j = 0; j < 32; ++j) {
+    if constexpr (OP == 1)  // s32 dot of +-1 codes -> -(Hamming distance), exact
+      v[j] = fmaf(__int2float_rn((int32_t)r[j]), 0.5f, p.dot_offset);
+    else
+      v[j] = __uint_as_float(r[j]);
+  }
+  if (NBM == 0) {
+    const float4* nb4 = reinterpret_cast<const float4*>(nbs);
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      float4 t = nb4[j4];
+      sub2(v[4 * j4 + 0], v[4 * j4 + 1], t.x, t.y);
+      sub2(v[4 * j4 + 2], v[4 * j4 + 3], t.z, t.w);
     }
+  }
+  const float lo = max3(max3(max3(v[0], v[1], v[2]), max3(v[3], v[4], v[5]),
+                             max3(v[6], v[7], v[8])),
+                        max3(max3(v[9], v[10], v[11]), max3(v[12], v[13], v[14]), v[15]),
+                        -INFINITY);
+  const float hi = max3(max3(max3(v[16], v[17], v[18]), max3(v[19], v[20], v[21]),
+                             max3(v[22], v[23], v[24])),
+                        max3(max3(v[25], v[26], v[27]), max3(v[28], v[29], v[30]), v[31]),
+                        -INFINITY);
+  const bool a_lo = row_on && lo >= st.thr;
+  if (__any_sync(0xffffffffu, a_lo || (row_on && hi >= st.thr))) {
+    epi_slow_list16<KR, MODE>(v, a_lo, col0, p, key, sv, st);
+    // the floor may have risen with the first half
+    epi_slow_list16<KR, MODE>(v + 16, row_on && hi >= st.thr, col0 + 16, p, key, sv, st);
   }
 }
 
@@ -707,8 +761,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR, OP, MODE>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
+          if constexpr (KR > 0 && NBM == 1 && MODE == 0) {
+            epi_sub32<NBM, KR, OP, MODE>(ra, nbw + c * 32, col_base + c * 32, p, row_on, key, sv, st);
+          } else {
+            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
+          }
           __syncwarp();
           tmem_wait_ld_regs(rb);
           if (c + 2 < NCH) {
@@ -718,8 +776,12 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
-          epi_sub16<HS, NBM, KR, OP, MODE>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
-          epi_sub16<HS, NBM, KR, OP, MODE>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
+          if constexpr (KR > 0 && NBM == 1 && MODE == 0) {
+            epi_sub32<NBM, KR, OP, MODE>(rb, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, key, sv, st);
+          } else {
+            epi_sub16<HS, NBM, KR, OP, MODE>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP, MODE>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
+          }
           if (c + 2 < NCH) {
             __syncwarp();
             tmem_wait_ld_regs(ra);
