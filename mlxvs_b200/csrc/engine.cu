@@ -205,7 +205,10 @@ void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
   int64_t blocks = std::min<int64_t>((p.n_pad + 7) / 8, (int64_t)sms * 16);
   bool vec = p.d % 4 == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
   ProfScope prof("prep", s);
-  if (vec && p.lo == nullptr && !p.cosine)
+  if (vec && p.lo == nullptr && !p.cosine && p.d_pad <= 128) {
+    const int64_t blocks4 = std::min<int64_t>((p.n_pad + 31) / 32, (int64_t)sms * 16);
+    prep_rows4_kernel<<<(unsigned)blocks4, threads, 0, s>>>(p);
+  } else if (vec && p.lo == nullptr && !p.cosine)
     prep_rows_vec4_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(p);
   else if (vec)
     prep_rows_vec4_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(p);

@@ -266,6 +266,86 @@ __global__ void prep_rows_vec4_kernel(const PrepParams p) {
   }
 }
 
+// The plain case (no cosine, no split plane) for rows of at most 128 values
+// (d_pad <= 128): each warp converts four rows per step with its lanes' four
+// float4 loads in flight together, then four interleaved warp sums.  Same
+// outputs as prep_rows_vec4_kernel<false>, row for row.
+__global__ void prep_rows4_kernel(const PrepParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  uint32_t inexact = 0, unfoldable = 0;
+  float amax = 0.0f;
+  float wmax = 0.0f;
+  const int d4 = p.d >> 2;
+  const int dp4 = p.d_pad >> 2;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t warp_id = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t r0 = warp_id * 4; r0 < p.n_pad; r0 += warps * 4) {
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = r0 + i;
+      v[i] = (row < p.n && lane < d4)
+                 ? __ldg(reinterpret_cast<const float4*>(p.x + (size_t)row * p.d) + lane)
+                 : zero4;
+    }
+    float ss[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = r0 + i;
+      float ss_main = 0.0f;
+      ss_main += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+      ss[i] = ss_main;
+      if (row < p.n_pad && lane < dp4) {
+        float w0 = v[i].x * p.mul, w1 = v[i].y * p.mul, w2 = v[i].z * p.mul, w3 = v[i].w * p.mul;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(w0), fabsf(w1)), fmaxf(fabsf(w2), fabsf(w3))));
+        w0 *= p.scale;
+        w1 *= p.scale;
+        w2 *= p.scale;
+        w3 *= p.scale;
+        __half2 h01 = __floats2half2_rn(w0, w1);
+        __half2 h23 = __floats2half2_rn(w2, w3);
+        const float2 b01 = __half22float2(h01), b23 = __half22float2(h23);
+        uint2 out;
+        out.x = *reinterpret_cast<uint32_t*>(&h01);
+        out.y = *reinterpret_cast<uint32_t*>(&h23);
+        reinterpret_cast<uint2*>(p.hi + (size_t)row * p.d_pad)[lane] = out;
+        if (b01.x != w0 || b01.y != w1 || b23.x != w2 || b23.y != w3) inexact = 1;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t row = r0 + i;
+        if (row >= p.n_pad) break;
+        if (row >= p.n) {
+          if (p.norm_out) p.norm_out[row] = p.pad_norm;
+          if (p.xp) write_pieces(p.xp, row, 0.0f, false);
+          continue;
+        }
+        if (p.norm_out) p.norm_out[row] = p.norm_scale == 0.0f ? 0.0f : ss[i] * p.norm_scale;
+        if (p.xp) unfoldable |= write_pieces(p.xp, row, ss[i], true);
+        if (p.rownorm_max) wmax = fmaxf(wmax, ss[i] * p.mul * p.mul);
+      }
+    }
+  }
+  if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
+  if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
+  if (p.flags) {
+    inexact = __any_sync(0xffffffffu, inexact);
+    amax = warp_max(amax);
+    if (lane == 0) {
+      if (inexact) atomicOr(p.flags, 1u);
+      atomicMax(p.flags + 1, __float_as_uint(amax));
+    }
+  }
+}
+
 // |q|^2 per query in float32 (src/knn.cpp:123), one warp per row.
 __global__ void row_sumsq_kernel(const float* x, int64_t n, int32_t d, float* out) {
   const int lane = threadIdx.x & 31;
