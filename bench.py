@@ -10,8 +10,9 @@ A step is one exact search of every query against the whole base: the
 fp32 -> fp16 input conversion, the fused tcgen05 distance + top-k kernel,
 (for N > 1) the NCCL all-gather of each rank's [nq, k] candidates, and the
 merge to ids and distances.  `value` is whole-job queries/s with the inputs
-resident in HBM (the fp32 base, 512 MB, is larger than L2, so no flush is
-needed); `e2e` is the same through the host-memory API, copies included.
+resident in HBM, L2 flushed before every timed step (a rank's shard is
+smaller than L2 at 8 GPUs); `e2e` is the same through the host-memory API,
+copies included.
 Inputs are seeded synthetic data with BASELINE's distributions.
 """
 
@@ -74,6 +75,8 @@ WORKLOADS = {
                               desc="config 4: 10M x 1024-bit codes, 10k queries, k=10"),
 }
 DEFAULT_WORKLOAD = "knn-l2-1m-k10"
+# twice the B200's 126 MB L2
+FLUSH_BYTES = 256 << 20
 METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pipe roofline"
 
 # DRAM bytes per launch of the dominant kernel, from the committed ncu
@@ -413,24 +416,32 @@ def main():
     sampler = ClockSampler(gpu_id) if rank == 0 else None
     if sampler:
         sampler.start()
+    # L2 (126 MB) is flushed before every timed step by writing a buffer of
+    # twice its size: a rank's shard is smaller than L2 from N = 8 on (64 MB
+    # of fp32 rows), so "inputs larger than L2" would not hold at every N.
+    # Each step is timed alone with CUDA events on the launching stream, the
+    # flushes between the spans; the step time is the sum of the spans.
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    spans = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        flush.fill_(i & 0x7F)
+        spans[i][0].record(stream)
         ids, dist_out = step()
-    t1.record(stream)
+        spans[i][1].record(stream)
     torch.cuda.synchronize()
     barrier()
-    elapsed_ms = t0.elapsed_time(t1)
+    elapsed_ms = sum(a.elapsed_time(b) for a, b in spans)
     clocks = sampler.stop() if sampler else None
     # per-kernel times from CUDA events around each launch, in a separate
     # pass of the same steps (the events would otherwise add about 1 % to
     # the timed steps)
     prof_steps = min(args.steps, 20)
     mv.profile_enable(True)
-    for _ in range(prof_steps):
+    for i in range(prof_steps):
+        flush.fill_(i & 0x7F)
         step()
     torch.cuda.synchronize()
     kname = "hamming_topk" if is_hamming else "gemm_topk"
@@ -603,8 +614,8 @@ def main():
                        "parallelism": (f"rows to list split over {world} GPU(s), all rows on "
                                        f"each" if is_allnn else
                                        f"base rows sharded over {world} GPU(s)"),
-                       "l2_flush": "inputs larger than L2 (fp32 base 512 MB)"
-                       if not is_hamming else "inputs larger than L2"},
+                       "l2_flush": f"{FLUSH_BYTES >> 20} MiB buffer written before every "
+                                   f"timed step (outside the per-step event spans)"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(all_launches), "clocks": clocks,
             "check_vs_oracle_4_queries": check,

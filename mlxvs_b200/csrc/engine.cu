@@ -120,6 +120,40 @@ struct ProfScope {
   }
 };
 
+// A speculative launch is recorded as PROF_SPECULATIVE until the host knows
+// whether it did the work: then as `kept_as`, or as PROF_SKIPPED (a launch
+// that returned at entry, with no issued work).
+constexpr const char* PROF_SPECULATIVE = "gemm_topk_speculative";
+constexpr const char* PROF_SKIPPED = "gemm_topk_skipped";
+void profile_resolve_speculative(const char* kept_as) {
+  std::lock_guard<std::mutex> g(prof_mu);
+  for (auto it = prof_records.rbegin(); it != prof_records.rend(); ++it) {
+    if (std::strcmp(it->name, PROF_SPECULATIVE) != 0) continue;
+    it->name = kept_as ? kept_as : PROF_SKIPPED;
+    if (!kept_as) it->issued = 0.0;
+    return;
+  }
+}
+
+// The flags of a call's prep read back through pinned memory: one buffer and
+// one event per (host thread, device), so a call waits for the copy alone
+// while the kernels enqueued after it keep running.
+struct FlagMailbox {
+  uint32_t* host = nullptr;
+  cudaEvent_t ev = nullptr;
+};
+FlagMailbox& flag_mailbox() {
+  thread_local FlagMailbox boxes[64];
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  FlagMailbox& b = boxes[dev];
+  if (b.host == nullptr) {
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&b.host), 64, cudaHostAllocDefault));
+    CK(cudaEventCreateWithFlags(&b.ev, cudaEventDisableTiming));
+  }
+  return b;
+}
+
 // Scratch buffers of one call, returned to the pool in stream order.
 struct Scratch {
   cudaStream_t s;
@@ -264,10 +298,12 @@ struct GemmMaps {
 
 template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0, int MODE = 0>
 void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t smem,
-                 cudaStream_t s) {
+                 cudaStream_t s, const char* prof_name = nullptr) {
   auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP, MODE>;
   CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ProfScope prof(OP == 1 ? "hamming_mma" : (MODE == 1 ? "gemm_collect" : "gemm_topk"), s);
+  ProfScope prof(prof_name ? prof_name
+                           : (OP == 1 ? "hamming_mma" : (MODE == 1 ? "gemm_collect" : "gemm_topk")),
+                 s);
   // every (query block, tile) pair runs 128 x 256 MMAs over the issued K:
   // NPASS fp16 products per 64-column chunk plus the K=16 |b|^2 block, or
   // 128 int8 columns per chunk
@@ -632,6 +668,102 @@ bool approx_search(const float* base, int64_t n, const float* queries, int64_t n
                         qq, out_keys, ids, dist, 1.0f, sc, s, &rs, eps);
 }
 
+// Scratch, tensor maps and parameters of one fused launch over (query block,
+// base range) units: npa operand planes (1: the inputs exactly in fp16, 2:
+// split hi / lo), fold: -|b|^2 rides in the MMA as one more K step, nbm: the
+// accumulator is the score (else the epilogue subtracts nb).
+struct FusedPlan {
+  GemmShape shape;
+  GemmMaps maps;
+  KnnGemmParams p;
+  uint64_t* partial;
+  int grid;
+  uint32_t smem;
+};
+
+FusedPlan plan_fused(const DeviceInfo& dev, int npa, bool fold, int nbm, int kchunks, int k,
+                     int64_t nq, int64_t n_pad, int64_t nq_pad, int d_pad, const __half* q_hi,
+                     const __half* q_lo, const __half* b_hi, const __half* b_lo,
+                     const __half* b_x, const float* nb, int64_t n, int64_t id_offset,
+                     int64_t self_base, Scratch& sc, cudaStream_t s) {
+  FusedPlan f{};
+  f.shape = choose_shape(dev, npa, kchunks, k, fold ? 1 : 0, nbm, npa == 1 ? 4 : 2);
+  const int QB = f.shape.qb;
+  const int qblocks = (int)((nq + QB - 1) / QB);
+  const int tiles = (int)(n_pad / GT_BN);
+  const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
+  const int units = qblocks * splits;
+
+  f.partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
+  unsigned long long* gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
+  CK(cudaMemsetAsync(gfloor, 0, (size_t)nq_pad * 8, s));
+  int* done = sc.alloc<int>((size_t)qblocks);
+  CK(cudaMemsetAsync(done, 0, (size_t)qblocks * 4, s));
+
+  f.maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, QB);
+  f.maps.a_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, QB);
+  f.maps.b_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  f.maps.b_lo = map_f16(b_lo ? b_lo : b_hi, d_pad, n_pad, GT_KCH, GT_BN);
+  f.maps.b_x = fold ? map_f16(b_x, 16, n_pad, 16, GT_BN, CU_TENSOR_MAP_SWIZZLE_32B) : f.maps.b_hi;
+
+  KnnGemmParams& p = f.p;
+  p.qblocks = qblocks;
+  p.tiles = tiles;
+  p.splits = splits;
+  p.units = units;
+  p.kchunks = kchunks;
+  p.k = k;
+  p.stages = f.shape.stages;
+  p.a_stream = f.shape.a_stream;
+  p.extra = fold ? 1 : 0;
+  p.n_valid = n;
+  p.nq = nq;
+  p.nq_pad = nq_pad;
+  p.id_offset = id_offset;
+  p.nb = nb;
+  p.partial = f.partial;
+  p.gfloor = gfloor;
+  p.done = done;
+  p.self_base = self_base;
+  p.tile_stride = 1;
+  p.err = dev.err;
+  p.wait_ns = WAIT_LIMIT_NS;
+  const GemmSmem lay = gemm_smem(QB, npa, f.shape.cg, kchunks, f.shape.stages, f.shape.a_stream,
+                                 k, fold, f.shape.kr, nbm);
+  f.smem = lay.total + 1024u;
+  f.grid = std::min(units, dev.sms);
+  return f;
+}
+
+// The fused kernel of a plan: exact (one fp16 pass) or three split passes.
+void launch_fused(const FusedPlan& f, bool exact, int nbm, cudaStream_t s,
+                  const char* prof_name = nullptr) {
+  const int QB = f.shape.qb, CG = f.shape.cg, KR = f.shape.kr;
+#define MLXVS_GEMM(QB_, CG_, KR_)                                                  \
+  if (QB == QB_ && CG == CG_ && KR == KR_) {                                       \
+    if (exact && nbm)                                                            \
+      launch_gemm<QB_, 1, CG_, 1, KR_>(f.maps, f.p, f.grid, f.smem, s, prof_name); \
+    else if (exact)                                                              \
+      launch_gemm<QB_, 1, CG_, 0, KR_>(f.maps, f.p, f.grid, f.smem, s, prof_name); \
+    else if (nbm)                                                                \
+      launch_gemm<QB_, 3, CG_, 1, KR_>(f.maps, f.p, f.grid, f.smem, s, prof_name); \
+    else                                                                         \
+      launch_gemm<QB_, 3, CG_, 0, KR_>(f.maps, f.p, f.grid, f.smem, s, prof_name); \
+  }
+  MLXVS_GEMM(128, 2, 8)
+  MLXVS_GEMM(128, 2, 10)
+  MLXVS_GEMM(128, 2, 12)
+  MLXVS_GEMM(128, 2, 16)
+  MLXVS_GEMM(128, 2, 32)
+  MLXVS_GEMM(128, 2, 0)
+  MLXVS_GEMM(128, 1, 0)
+  MLXVS_GEMM(64, 1, 0)
+  MLXVS_GEMM(32, 1, 0)
+  MLXVS_GEMM(16, 1, 0)
+  MLXVS_GEMM(8, 1, 0)
+#undef MLXVS_GEMM
+}
+
 // The exact k-NN of queries among base: keys [nq, k] (out_keys) and / or ids
 // and distances.  The per-call flow:
 //   1. prep: fp32 -> fp16 operand rows (2q for L2), |b|^2, |q|^2, and whether
@@ -684,14 +816,39 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
                 nullptr, qq, 1.0f, 0.0f, flags + 2, nullptr, nullptr, flags + 6};
   launch_prep(pb, dev.sms, s);
   launch_prep(pq, dev.sms, s);
+  FlagMailbox& mb = flag_mailbox();
+  CK(cudaMemcpyAsync(mb.host, flags, 32, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(mb.ev, s));
+  // k <= 16 (register lists), L2 or inner product: the one-pass search on
+  // exact operands (for L2 with -|b|^2 in the MMA) is launched before the
+  // flags are read, so the GPU does not wait for the host; its CTAs return
+  // at entry when the flags rule it out.  Cosine rows are unit rows, hardly
+  // ever exact in fp16, so they do not speculate.
+  const bool spec = k <= 16 && !cosine;
+  FusedPlan sp{};
+  if (spec) {
+    sp = plan_fused(dev, 1, l2, 1, kchunks, k, nq, n_pad, nq_pad, d_pad, q_hi, nullptr, b_hi,
+                    nullptr, b_x, nb, n, id_offset, self_base, sc, s);
+    sp.p.skip_if = flags;
+    launch_fused(sp, true, 1, s, PROF_SPECULATIVE);
+  }
+  CK(cudaEventSynchronize(mb.ev));
   uint32_t hflags[8];
-  CK(cudaMemcpyAsync(hflags, flags, 32, cudaMemcpyDeviceToHost, s));
-  CK(cudaStreamSynchronize(s));
+  std::memcpy(hflags, mb.host, 32);
   const bool exact = hflags[0] == 0 && hflags[2] == 0;
   // L2 on exact operands with integer |b|^2 < 2^31: -|b|^2 rides in the MMA
   // and the epilogue reads scores straight from the accumulator
   const bool fold = l2 && exact && hflags[4] == 0;
   const int nbm = (!l2 || fold) ? 1 : 0;
+  if (spec) {
+    // the device made the same decision from the same words
+    const bool kept = exact && (fold || !l2);
+    profile_resolve_speculative(kept ? "gemm_topk" : nullptr);
+    if (kept) {
+      launch_merge(sp.partial, sp.p.splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s);
+      return;
+    }
+  }
 
   __half* b_lo = nullptr;
   __half* q_lo = nullptr;
@@ -750,79 +907,13 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   }
 
   const int npa = exact ? 1 : 2;
-  const GemmShape shape = choose_shape(dev, npa, kchunks, k, fold ? 1 : 0, nbm, exact ? 4 : 2);
-  const int QB = shape.qb, CG = shape.cg, KR = shape.kr, stages = shape.stages,
-            a_stream = shape.a_stream;
-  const int qblocks = (int)((nq + QB - 1) / QB);
-  const int tiles = (int)(n_pad / GT_BN);
-  const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
-  const int units = qblocks * splits;
-
-  uint64_t* partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
-  unsigned long long* gfloor = sc.alloc<unsigned long long>((size_t)nq_pad);
-  CK(cudaMemsetAsync(gfloor, 0, (size_t)nq_pad * 8, s));
-  int* done = sc.alloc<int>((size_t)qblocks);
-  CK(cudaMemsetAsync(done, 0, (size_t)qblocks * 4, s));
-
-  GemmMaps maps;
-  maps.a_hi = map_f16(q_hi, d_pad, nq_pad, GT_KCH, QB);
-  maps.a_lo = map_f16(q_lo ? q_lo : q_hi, d_pad, nq_pad, GT_KCH, QB);
-  maps.b_hi = map_f16(b_hi, d_pad, n_pad, GT_KCH, GT_BN);
-  maps.b_lo = map_f16(b_lo ? b_lo : b_hi, d_pad, n_pad, GT_KCH, GT_BN);
-  maps.b_x = fold ? map_f16(b_x, 16, n_pad, 16, GT_BN, CU_TENSOR_MAP_SWIZZLE_32B) : maps.b_hi;
-
-  KnnGemmParams p{};
-  p.qblocks = qblocks;
-  p.tiles = tiles;
-  p.splits = splits;
-  p.units = units;
-  p.kchunks = kchunks;
-  p.k = k;
-  p.stages = stages;
-  p.a_stream = a_stream;
-  p.extra = fold ? 1 : 0;
-  p.n_valid = n;
-  p.nq = nq;
-  p.nq_pad = nq_pad;
-  p.id_offset = id_offset;
-  p.nb = nb;
-  p.partial = partial;
-  p.gfloor = gfloor;
-  p.done = done;
-  p.self_base = self_base;
-  p.tile_stride = 1;
-  p.err = dev.err;
-  p.wait_ns = WAIT_LIMIT_NS;
-  if (k > 16 && large_k_search(maps, p, exact, nbm, npa, kchunks, fold, q_hi, q_lo, nq_pad,
+  FusedPlan f = plan_fused(dev, npa, fold, nbm, kchunks, k, nq, n_pad, nq_pad, d_pad, q_hi, q_lo,
+                           b_hi, b_lo, b_x, nb, n, id_offset, self_base, sc, s);
+  if (k > 16 && large_k_search(f.maps, f.p, exact, nbm, npa, kchunks, fold, q_hi, q_lo, nq_pad,
                                 d_pad, mi, qq, out_keys, ids, dist, out_scale, sc, s))
     return;
-  const GemmSmem lay = gemm_smem(QB, npa, CG, kchunks, stages, a_stream, k, fold, KR, nbm);
-  const uint32_t smem = lay.total + 1024u;
-  const int grid = std::min(units, dev.sms);
-#define MLXVS_GEMM(QB_, CG_, KR_)                                           \
-  if (QB == QB_ && CG == CG_ && KR == KR_) {                                \
-    if (exact && nbm)                                                     \
-      launch_gemm<QB_, 1, CG_, 1, KR_>(maps, p, grid, smem, s);           \
-    else if (exact)                                                       \
-      launch_gemm<QB_, 1, CG_, 0, KR_>(maps, p, grid, smem, s);           \
-    else if (nbm)                                                         \
-      launch_gemm<QB_, 3, CG_, 1, KR_>(maps, p, grid, smem, s);           \
-    else                                                                  \
-      launch_gemm<QB_, 3, CG_, 0, KR_>(maps, p, grid, smem, s);           \
-  }
-  MLXVS_GEMM(128, 2, 8)
-  MLXVS_GEMM(128, 2, 10)
-  MLXVS_GEMM(128, 2, 12)
-  MLXVS_GEMM(128, 2, 16)
-  MLXVS_GEMM(128, 2, 32)
-  MLXVS_GEMM(128, 2, 0)
-  MLXVS_GEMM(128, 1, 0)
-  MLXVS_GEMM(64, 1, 0)
-  MLXVS_GEMM(32, 1, 0)
-  MLXVS_GEMM(16, 1, 0)
-  MLXVS_GEMM(8, 1, 0)
-#undef MLXVS_GEMM
-  launch_merge(partial, splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s, out_scale);
+  launch_fused(f, exact, nbm, s);
+  launch_merge(f.partial, f.p.splits, nq_pad, nq, k, mi, qq, out_keys, ids, dist, s, out_scale);
 }
 
 // ------------------------------------------------------------------ Hamming

@@ -82,6 +82,11 @@ struct KnnGemmParams {
   int64_t self_base;
   uint32_t* err;                   // error word (bounded waits that gave up)
   uint64_t wait_ns;                // limit of every wait
+  // non-null: a launch made before the host has read the prep's flags;
+  // every CTA returns at entry when skip_if[0] | skip_if[2] | skip_if[4] is
+  // non-zero (an operand is not exactly fp16, or |b|^2 cannot ride in the
+  // MMA), and the host then runs the search the flags call for
+  const uint32_t* skip_if;
 };
 
 // NBM = 0: the epilogue subtracts the per-row term nb from each dot (L2 when
@@ -432,6 +437,10 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+
+  // every thread reads the same words, written by the prep kernels earlier
+  // in the stream: the whole CTA returns, before any barrier or TMEM use
+  if (p.skip_if != nullptr && (p.skip_if[0] | p.skip_if[2] | p.skip_if[4]) != 0u) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {

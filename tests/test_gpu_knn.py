@@ -55,6 +55,23 @@ def test_integer_data_bit_exact(metric, k):
     assert np.array_equal(dist, odist)
 
 
+@pytest.mark.parametrize("metric", ["l2", "inner_product"])
+@pytest.mark.parametrize("k", [1, 10, 16])
+def test_exact_fp16_values_with_fractional_norms(metric, k):
+    # quarter steps in [0, 64): every value is exactly an fp16 and every
+    # float32 product and sum is exact, but |b|^2 is not an integer, so for
+    # L2 it cannot ride in the MMA and the search that was launched before
+    # the prep's flags were read must step aside (inner product keeps it)
+    b, q = data.gaussian_mixture_int(30_000, 128, 32, seed=11, nq=300)
+    b = (b * 0.25).astype(np.float32)
+    q = (q * 0.25).astype(np.float32)
+    for _ in range(2):
+        ids, dist = mv.brute_force_knn(b, q, k, metric)
+        oids, odist = O.brute_force_knn(b, q, k, metric)
+        assert np.array_equal(ids, oids)
+        assert np.array_equal(dist, odist)
+
+
 @pytest.mark.parametrize("d", [8, 48, 100, 130, 200, 300])
 def test_integer_data_odd_dims(d):
     b, q = data.gaussian_mixture_int(5_000 + 17, d, 8, seed=d, nq=77)
