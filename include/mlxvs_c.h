@@ -106,8 +106,10 @@ MLXVS_C_API int mlxvs_hamming_knn(
  * Replaces: mlxvs::brute_force_knn, include/mlxvs/mlxvs.h:59-65 (the C++
  * entry the Python binding python/bindings.cpp:37-47 calls).  The inputs
  * stay untouched; scratch memory comes from the device's stream-ordered
- * pool.  Synchronizes with the host once, after the input-conversion
- * kernels, to choose the exact fp16 path or the split-fp16 path.
+ * pool.  Waits once on the host for the input-conversion kernels' flags
+ * (exact fp16 operands or not); for k <= 16 with L2 or inner product the
+ * exact path's kernel is already enqueued behind them while the host waits,
+ * and returns at once if the flags call for another path.
  */
 MLXVS_C_API int mlxvs_brute_force_knn_device(
     const float* base,

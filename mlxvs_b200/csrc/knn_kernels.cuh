@@ -334,14 +334,33 @@ __global__ void prep_rows4_kernel(const PrepParams p) {
       }
     }
   }
-  if (p.rownorm_max && lane == 0) atomicMax(p.rownorm_max, __float_as_uint(wmax));
-  if (p.fold_flag && __any_sync(0xffffffffu, unfoldable) && lane == 0) atomicOr(p.fold_flag, 1u);
-  if (p.flags) {
-    inexact = __any_sync(0xffffffffu, inexact);
-    amax = warp_max(amax);
-    if (lane == 0) {
-      if (inexact) atomicOr(p.flags, 1u);
-      atomicMax(p.flags + 1, __float_as_uint(amax));
+  // the warps' flags and maxima meet in shared memory: one atomic per block
+  // and word instead of one per warp (thousands on the same addresses)
+  __shared__ float s_wmax[32], s_amax[32];
+  __shared__ uint32_t s_bits[32];
+  const int warp = threadIdx.x >> 5;
+  inexact = __any_sync(0xffffffffu, inexact);
+  unfoldable = __any_sync(0xffffffffu, unfoldable);
+  amax = warp_max(amax);
+  if (lane == 0) {
+    s_wmax[warp] = wmax;
+    s_amax[warp] = amax;
+    s_bits[warp] = (inexact ? 1u : 0u) | (unfoldable ? 2u : 0u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bw = 0.0f, ba = 0.0f;
+    uint32_t bits = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      bw = fmaxf(bw, s_wmax[w]);
+      ba = fmaxf(ba, s_amax[w]);
+      bits |= s_bits[w];
+    }
+    if (p.rownorm_max) atomicMax(p.rownorm_max, __float_as_uint(bw));
+    if (p.fold_flag && (bits & 2u)) atomicOr(p.fold_flag, 1u);
+    if (p.flags) {
+      if (bits & 1u) atomicOr(p.flags, 1u);
+      atomicMax(p.flags + 1, __float_as_uint(ba));
     }
   }
 }
@@ -531,6 +550,85 @@ __global__ void __launch_bounds__(256)
           }
           dist[(size_t)q * k + o] = dv;
         }
+      }
+    }
+  }
+}
+
+// At most this many candidates per query for merge_keys_lane_kernel (its
+// 32 queries' lists fill 48 KB of shared memory).
+constexpr int MERGE_LANE_MAX = 192;
+
+// The same merge with one lane per query, for k <= KR <= 32 and at most
+// MERGE_LANE_MAX candidates per query: the warp copies its 32 queries' rows
+// of every list into shared memory (each list's rows are contiguous, so the
+// copies are coalesced and all in flight at once), then each lane keeps its
+// query's k best in a sorted register list (list_insert), skipping a key it
+// already holds (a key present in two lists is taken once).  The same
+// result as merge_keys_warp_kernel with a sixth of its instructions: no
+// warp-wide argmax per output slot.
+template <int KR>
+__global__ void __launch_bounds__(32)
+    merge_keys_lane_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
+                           int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
+                           const float* __restrict__ qq, uint64_t* __restrict__ out_keys,
+                           int32_t* __restrict__ ids, float* __restrict__ dist, float scale) {
+  extern __shared__ __align__(16) uint64_t stage[];  // [num_lists][32][k]
+  const int lane = threadIdx.x;
+  const int64_t q0 = (int64_t)blockIdx.x * 32;
+  const int rows = (int)(nq - q0 < 32 ? nq - q0 : 32);
+  const int per_list = rows * k;
+  for (int l = 0; l < num_lists; ++l) {
+    const uint64_t* src = lists + ((size_t)l * list_rows + q0) * k;
+    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(stage + (size_t)l * 32 * k);
+    for (int i = lane; i < per_list; i += 32)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst + 8u * (uint32_t)i),
+                   "l"(src + i)
+                   : "memory");
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  __syncwarp();
+  if (lane >= rows) return;
+  const int64_t q = q0 + lane;
+  // ascending: key[0] the worst kept (0 while fewer than k are held); slots
+  // k .. KR-1 hold ~0 and never change
+  uint64_t key[KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) key[i] = i < k ? 0ull : ~0ull;
+  const uint64_t* mine = stage + (size_t)lane * k;
+  for (int l = 0; l < num_lists; ++l) {
+    const uint64_t* row = mine + (size_t)l * 32 * k;
+    for (int j = 0; j < k; ++j) {
+      const uint64_t x = row[j];
+      if (x <= key[0]) continue;
+      bool held = false;
+#pragma unroll
+      for (int i = 0; i < KR; ++i) held |= i < k && key[i] == x;
+      if (!held) list_insert<KR>(key, x);
+    }
+  }
+  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    if (i >= k) break;
+    const int o = k - 1 - i;  // best first
+    uint64_t kk = key[i];
+    const float sc = key_score(kk) * scale;
+    if (kk != 0 && scale != 1.0f) kk = make_key(sc, ~(uint32_t)kk);
+    if (out_keys) out_keys[(size_t)q * k + o] = kk;
+    if (ids) {
+      const int32_t id = key_id(kk);
+      ids[(size_t)q * k + o] = id;
+      if (dist) {
+        float dv;
+        if (kind == 1) {
+          dv = id >= 0 ? fmaxf(qn - sc, 0.0f) : INFINITY;
+        } else if (kind == 3) {
+          dv = id >= 0 ? -sc : INFINITY;
+        } else {
+          dv = id >= 0 ? sc : -INFINITY;
+        }
+        dist[(size_t)q * k + o] = dv;
       }
     }
   }

@@ -97,3 +97,32 @@ def test_refine_device_missing_and_errors():
     with pytest.raises(ValueError, match="must match"):
         mv.refine(x, q[:, :5], cand, 3, "l2")
     mv.synchronize()
+
+
+@pytest.mark.parametrize("k,lists,nq", [(1, 7, 45), (4, 30, 100), (5, 2, 33), (10, 13, 10_000),
+                                        (10, 19, 77), (10, 20, 70), (16, 12, 64), (17, 5, 31),
+                                        (32, 6, 50), (32, 7, 40)])
+def test_merge_keys_duplicates_and_empty_slots(k, lists, nq):
+    # the candidate lists of the units or ranks of one search: a key may sit
+    # in several lists (units start from an earlier unit's list), slots may
+    # be empty (0), the lists need not be sorted; up to 192 candidates per
+    # query take the lane-per-query merge, more the warp-per-query one
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(1000 * k + lists)
+    table = rng.integers(-40, 40, size=(nq, 300)).astype(np.float32)
+    ids = rng.integers(0, 300, size=(lists, nq, k))
+    scores = np.take_along_axis(table[None].repeat(lists, 0), ids, axis=2)
+    keys = (O._order_bits(scores).astype(np.uint64) << np.uint64(32)) | \
+        (~ids.astype(np.uint32)).astype(np.uint64)
+    keys[rng.random(keys.shape) < 0.2] = 0
+    # expected: the k largest distinct non-zero keys per query, best first
+    okeys = np.zeros((nq, k), np.uint64)
+    for i in range(nq):
+        u = np.unique(keys[:, i, :])[::-1]
+        u = u[u != 0][:k]
+        okeys[i, :len(u)] = u
+    oids, oscores = O.decode_keys(okeys)
+    t = torch.from_numpy(keys.view(np.int64)).cuda()
+    gids, gdist = mv.merge_keys(t, k, "inner_product")
+    assert np.array_equal(gids.cpu().numpy(), oids)
+    assert np.array_equal(gdist.cpu().numpy(), oscores)
