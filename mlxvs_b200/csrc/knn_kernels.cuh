@@ -559,15 +559,43 @@ __global__ void __launch_bounds__(256)
 // 32 queries' lists fill 48 KB of shared memory).
 constexpr int MERGE_LANE_MAX = 192;
 
-// The same merge with one lane per query, for k <= KR <= 32 and at most
-// MERGE_LANE_MAX candidates per query: the warp copies its 32 queries' rows
-// of every list into shared memory (each list's rows are contiguous, so the
-// copies are coalesced and all in flight at once), then each lane keeps its
-// query's k best in a sorted register list (list_insert), skipping a key it
-// already holds (a key present in two lists is taken once).  The same
-// result as merge_keys_warp_kernel with a sixth of its instructions: no
-// warp-wide argmax per output slot.
-template <int KR>
+// Writes output slot o of query q: the key (scores times scale) and / or
+// its id and distance of the given kind (see merge_keys).
+__device__ __forceinline__ void merge_write(uint64_t key, int64_t q, int o, int k, int kind,
+                                            float qn, float scale, uint64_t* out_keys,
+                                            int32_t* ids, float* dist) {
+  const float sc = key_score(key) * scale;
+  if (key != 0 && scale != 1.0f) key = make_key(sc, ~(uint32_t)key);
+  if (out_keys) out_keys[(size_t)q * k + o] = key;
+  if (ids) {
+    const int32_t id = key_id(key);
+    ids[(size_t)q * k + o] = id;
+    if (dist) {
+      float dv;
+      if (kind == 1) {
+        dv = id >= 0 ? fmaxf(qn - sc, 0.0f) : INFINITY;
+      } else if (kind == 3) {
+        dv = id >= 0 ? -sc : INFINITY;
+      } else {
+        dv = id >= 0 ? sc : -INFINITY;
+      }
+      dist[(size_t)q * k + o] = dv;
+    }
+  }
+}
+
+// The same merge with one lane per query, for k <= KR <= 32, at most SM <= 32
+// lists and at most MERGE_LANE_MAX candidates per query.  The warp copies
+// its 32 queries' rows of every list into shared memory (each list's rows
+// are contiguous, so the copies are coalesced and all in flight at once).
+// Then each lane checks its lists: when every one is sorted, best first or
+// best last, with empty slots (0) only at its worst end (the fused kernel's
+// register lists are written worst first, merged lists best first), the k
+// best are taken from the lists' heads, k rounds of a max over at most SM
+// heads, every head equal to the taken key moving on (a key present in two
+// lists is taken once).  Otherwise the lane keeps its query's k best in a
+// sorted register list (list_insert), skipping a key it already holds.
+template <int KR, int SM>
 __global__ void __launch_bounds__(32)
     merge_keys_lane_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
                            int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
@@ -590,14 +618,60 @@ __global__ void __launch_bounds__(32)
   __syncwarp();
   if (lane >= rows) return;
   const int64_t q = q0 + lane;
+  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
+  const uint64_t* mine = stage + (size_t)lane * k;
+  const size_t lstride = (size_t)32 * k;
+
+  // which lists run best last (ascending) and whether every list is sorted
+  uint32_t asc = 0;
+  bool sorted = true;
+  for (int l = 0; l < num_lists && sorted; ++l) {
+    const uint64_t* row = mine + l * lstride;
+    bool up = true, down = true;
+    uint64_t prev = row[0];
+    for (int j = 1; j < k; ++j) {
+      const uint64_t x = row[j];
+      const bool both0 = x == 0 && prev == 0;
+      up &= x > prev || both0;
+      down &= x < prev || both0;
+      prev = x;
+    }
+    if (up && !down) asc |= 1u << l;
+    sorted = up || down;
+  }
+
+  if (sorted) {
+    uint64_t head[SM];
+    int pos[SM];
+#pragma unroll
+    for (int l = 0; l < SM; ++l) {
+      pos[l] = ((asc >> l) & 1u) ? k - 1 : 0;
+      head[l] = l < num_lists ? mine[l * lstride + pos[l]] : 0ull;
+    }
+    for (int o = 0; o < k; ++o) {
+      uint64_t best = head[0];
+#pragma unroll
+      for (int l = 1; l < SM; ++l) best = head[l] > best ? head[l] : best;
+      merge_write(best, q, o, k, kind, qn, scale, out_keys, ids, dist);
+#pragma unroll
+      for (int l = 0; l < SM; ++l) {
+        if (best != 0 && head[l] == best) {
+          const bool up = (asc >> l) & 1u;
+          pos[l] += up ? -1 : 1;
+          head[l] = (pos[l] >= 0 && pos[l] < k) ? mine[l * lstride + pos[l]] : 0ull;
+        }
+      }
+    }
+    return;
+  }
+
   // ascending: key[0] the worst kept (0 while fewer than k are held); slots
   // k .. KR-1 hold ~0 and never change
   uint64_t key[KR];
 #pragma unroll
   for (int i = 0; i < KR; ++i) key[i] = i < k ? 0ull : ~0ull;
-  const uint64_t* mine = stage + (size_t)lane * k;
   for (int l = 0; l < num_lists; ++l) {
-    const uint64_t* row = mine + (size_t)l * 32 * k;
+    const uint64_t* row = mine + l * lstride;
     for (int j = 0; j < k; ++j) {
       const uint64_t x = row[j];
       if (x <= key[0]) continue;
@@ -607,30 +681,10 @@ __global__ void __launch_bounds__(32)
       if (!held) list_insert<KR>(key, x);
     }
   }
-  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
 #pragma unroll
   for (int i = 0; i < KR; ++i) {
     if (i >= k) break;
-    const int o = k - 1 - i;  // best first
-    uint64_t kk = key[i];
-    const float sc = key_score(kk) * scale;
-    if (kk != 0 && scale != 1.0f) kk = make_key(sc, ~(uint32_t)kk);
-    if (out_keys) out_keys[(size_t)q * k + o] = kk;
-    if (ids) {
-      const int32_t id = key_id(kk);
-      ids[(size_t)q * k + o] = id;
-      if (dist) {
-        float dv;
-        if (kind == 1) {
-          dv = id >= 0 ? fmaxf(qn - sc, 0.0f) : INFINITY;
-        } else if (kind == 3) {
-          dv = id >= 0 ? -sc : INFINITY;
-        } else {
-          dv = id >= 0 ? sc : -INFINITY;
-        }
-        dist[(size_t)q * k + o] = dv;
-      }
-    }
+    merge_write(key[i], q, k - 1 - i, k, kind, qn, scale, out_keys, ids, dist);
   }
 }
 

@@ -99,22 +99,37 @@ def test_refine_device_missing_and_errors():
     mv.synchronize()
 
 
+@pytest.mark.parametrize("order", ["random", "best_first", "worst_first", "mixed"])
 @pytest.mark.parametrize("k,lists,nq", [(1, 7, 45), (4, 30, 100), (5, 2, 33), (10, 13, 10_000),
                                         (10, 19, 77), (10, 20, 70), (16, 12, 64), (17, 5, 31),
-                                        (32, 6, 50), (32, 7, 40)])
-def test_merge_keys_duplicates_and_empty_slots(k, lists, nq):
+                                        (32, 6, 50), (32, 7, 40), (1, 40, 64)])
+def test_merge_keys_duplicates_and_empty_slots(k, lists, nq, order):
     # the candidate lists of the units or ranks of one search: a key may sit
     # in several lists (units start from an earlier unit's list), slots may
-    # be empty (0), the lists need not be sorted; up to 192 candidates per
-    # query take the lane-per-query merge, more the warp-per-query one
+    # be empty (0); lists come best first (merged lists), worst first with
+    # the empty slots in front (the fused kernel's register lists) or in no
+    # order (its heaps).  Up to 192 candidates in up to 32 lists per query
+    # take the lane-per-query merge, more the warp-per-query one.
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(1000 * k + lists)
     table = rng.integers(-40, 40, size=(nq, 300)).astype(np.float32)
-    ids = rng.integers(0, 300, size=(lists, nq, k))
+    if order == "random":  # ids may repeat inside a list too
+        ids = rng.integers(0, 300, size=(lists, nq, k))
+    else:
+        ids = np.argsort(rng.random((lists, nq, 300)), axis=2)[..., :k]
     scores = np.take_along_axis(table[None].repeat(lists, 0), ids, axis=2)
     keys = (O._order_bits(scores).astype(np.uint64) << np.uint64(32)) | \
         (~ids.astype(np.uint32)).astype(np.uint64)
     keys[rng.random(keys.shape) < 0.2] = 0
+    if order in ("best_first", "mixed"):
+        srt = np.sort(keys, axis=2)[..., ::-1]
+        if order == "mixed":
+            pick = rng.random(nq) < 0.5
+            keys[:, pick, :] = srt[:, pick, :]
+        else:
+            keys = srt.copy()
+    elif order == "worst_first":
+        keys = np.sort(keys, axis=2)
     # expected: the k largest distinct non-zero keys per query, best first
     okeys = np.zeros((nq, k), np.uint64)
     for i in range(nq):
@@ -122,7 +137,7 @@ def test_merge_keys_duplicates_and_empty_slots(k, lists, nq):
         u = u[u != 0][:k]
         okeys[i, :len(u)] = u
     oids, oscores = O.decode_keys(okeys)
-    t = torch.from_numpy(keys.view(np.int64)).cuda()
+    t = torch.from_numpy(keys.copy().view(np.int64)).cuda()
     gids, gdist = mv.merge_keys(t, k, "inner_product")
     assert np.array_equal(gids.cpu().numpy(), oids)
     assert np.array_equal(gdist.cpu().numpy(), oscores)
