@@ -256,29 +256,20 @@ void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64
                   cudaStream_t s, float scale = 1.0f) {
   if (nq == 0) return;
   int64_t total = (int64_t)num_lists * k;
-  if (k <= 32 && total <= MERGE_LANE_MAX && num_lists <= 32) {
+  if (k <= 32 && total <= MERGE_QUAD_MAX && num_lists <= 32) {
     ProfScope prof("merge", s);
-    const unsigned blocks = (unsigned)((nq + 31) / 32);
-    const size_t smem = (size_t)total * 32 * sizeof(uint64_t);
-#define MLXVS_MERGE_LANE(KR_, SM_)                                                    \
-  merge_keys_lane_kernel<KR_, SM_><<<blocks, 32, smem, s>>>(                            \
-      lists, num_lists, list_rows, nq, k, kind, qq, out_keys, ids, dist, scale)
-#define MLXVS_MERGE_LANE_K(SM_) \
-  if (k <= 10)                  \
-    MLXVS_MERGE_LANE(10, SM_);  \
-  else if (k <= 16)             \
-    MLXVS_MERGE_LANE(16, SM_);  \
-  else                          \
-    MLXVS_MERGE_LANE(32, SM_);
-    if (num_lists <= 8) {
-      MLXVS_MERGE_LANE_K(8)
-    } else if (num_lists <= 16) {
-      MLXVS_MERGE_LANE_K(16)
-    } else {
-      MLXVS_MERGE_LANE_K(32)
-    }
-#undef MLXVS_MERGE_LANE_K
-#undef MLXVS_MERGE_LANE
+    const unsigned blocks = (unsigned)((nq + 7) / 8);
+    const size_t smem = (size_t)total * 8 * sizeof(uint64_t);
+#define MLXVS_MERGE_QUAD(KR_)                                                              \
+  merge_keys_quad_kernel<KR_><<<blocks, 32, smem, s>>>(lists, num_lists, list_rows, nq, k, \
+                                                         kind, qq, out_keys, ids, dist, scale)
+    if (k <= 10)
+      MLXVS_MERGE_QUAD(10);
+    else if (k <= 16)
+      MLXVS_MERGE_QUAD(16);
+    else
+      MLXVS_MERGE_QUAD(32);
+#undef MLXVS_MERGE_QUAD
     CK(cudaGetLastError());
     return;
   }

@@ -555,9 +555,9 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// At most this many candidates per query for merge_keys_lane_kernel (its
-// 32 queries' lists fill 48 KB of shared memory).
-constexpr int MERGE_LANE_MAX = 192;
+// At most this many candidates per query for merge_keys_quad_kernel (its
+// 8 queries' lists fill 48 KB of shared memory).
+constexpr int MERGE_QUAD_MAX = 768;
 
 // Writes output slot o of query q: the key (scores times scale) and / or
 // its id and distance of the given kind (see merge_keys).
@@ -584,31 +584,33 @@ __device__ __forceinline__ void merge_write(uint64_t key, int64_t q, int o, int 
   }
 }
 
-// The same merge with one lane per query, for k <= KR <= 32, at most SM <= 32
-// lists and at most MERGE_LANE_MAX candidates per query.  The warp copies
-// its 32 queries' rows of every list into shared memory (each list's rows
-// are contiguous, so the copies are coalesced and all in flight at once).
-// Then each lane checks its lists: when every one is sorted, best first or
-// best last, with empty slots (0) only at its worst end (the fused kernel's
-// register lists are written worst first, merged lists best first), the k
-// best are taken from the lists' heads, k rounds of a max over at most SM
-// heads, every head equal to the taken key moving on (a key present in two
-// lists is taken once).  Otherwise the lane keeps its query's k best in a
-// sorted register list (list_insert), skipping a key it already holds.
-template <int KR, int SM>
+// The same merge with four lanes per query (eight queries per warp), for
+// k <= KR <= 32, at most 32 lists and at most MERGE_QUAD_MAX candidates per
+// query.  The warp copies its queries' rows of every list into shared
+// memory (each list's rows are contiguous, so the copies are coalesced and
+// all in flight at once).  Lane r of a query owns lists r, r + 4, ... .
+// When every list of the warp is sorted, best first or best last, with
+// empty slots (0) only at its worst end (the fused kernel's register lists
+// are written worst first, merged lists best first), each of the k output
+// slots is the best of the query's list heads (a max over a lane's heads,
+// then over the four lanes by two shuffles), and every head equal to it
+// moves on (a key present in two lists is taken once).  Otherwise the first
+// lane of each query keeps its k best in a sorted register list
+// (list_insert), skipping a key it already holds.
+template <int KR>
 __global__ void __launch_bounds__(32)
-    merge_keys_lane_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
+    merge_keys_quad_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
                            int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
                            const float* __restrict__ qq, uint64_t* __restrict__ out_keys,
                            int32_t* __restrict__ ids, float* __restrict__ dist, float scale) {
-  extern __shared__ __align__(16) uint64_t stage[];  // [num_lists][32][k]
+  extern __shared__ __align__(16) uint64_t stage[];  // [num_lists][8][k]
   const int lane = threadIdx.x;
-  const int64_t q0 = (int64_t)blockIdx.x * 32;
-  const int rows = (int)(nq - q0 < 32 ? nq - q0 : 32);
+  const int64_t q0 = (int64_t)blockIdx.x * 8;
+  const int rows = (int)(nq - q0 < 8 ? nq - q0 : 8);
   const int per_list = rows * k;
   for (int l = 0; l < num_lists; ++l) {
     const uint64_t* src = lists + ((size_t)l * list_rows + q0) * k;
-    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(stage + (size_t)l * 32 * k);
+    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(stage + (size_t)l * 8 * k);
     for (int i = lane; i < per_list; i += 32)
       asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst + 8u * (uint32_t)i),
                    "l"(src + i)
@@ -616,55 +618,67 @@ __global__ void __launch_bounds__(32)
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncwarp();
-  if (lane >= rows) return;
-  const int64_t q = q0 + lane;
-  const float qn = (kind == 1 && qq) ? qq[q] : 0.0f;
-  const uint64_t* mine = stage + (size_t)lane * k;
-  const size_t lstride = (size_t)32 * k;
+  const int g = lane >> 2;  // query of the warp
+  const int r = lane & 3;   // this lane's lists: r, r + 4, ...
+  const bool row_ok = g < rows;
+  const int64_t q = q0 + g;
+  const uint64_t* mine = stage + (size_t)g * k;
+  const size_t lstride = (size_t)8 * k;
 
-  // which lists run best last (ascending) and whether every list is sorted
+  // which of this lane's lists run best last (bit i: list r + 4 i), and
+  // whether every one is sorted
   uint32_t asc = 0;
   bool sorted = true;
-  for (int l = 0; l < num_lists && sorted; ++l) {
-    const uint64_t* row = mine + l * lstride;
-    bool up = true, down = true;
-    uint64_t prev = row[0];
-    for (int j = 1; j < k; ++j) {
-      const uint64_t x = row[j];
-      const bool both0 = x == 0 && prev == 0;
-      up &= x > prev || both0;
-      down &= x < prev || both0;
-      prev = x;
+  if (row_ok) {
+    for (int i = 0, l = r; l < num_lists && sorted; ++i, l += 4) {
+      const uint64_t* row = mine + l * lstride;
+      bool up = true, down = true;
+      uint64_t prev = row[0];
+      for (int j = 1; j < k; ++j) {
+        const uint64_t x = row[j];
+        const bool both0 = x == 0 && prev == 0;
+        up &= x > prev || both0;
+        down &= x < prev || both0;
+        prev = x;
+      }
+      if (up && !down) asc |= 1u << i;
+      sorted = up || down;
     }
-    if (up && !down) asc |= 1u << l;
-    sorted = up || down;
   }
+  const float qn = (kind == 1 && qq && row_ok) ? qq[q] : 0.0f;
 
-  if (sorted) {
-    uint64_t head[SM];
-    int pos[SM];
+  if (__all_sync(0xffffffffu, sorted)) {
+    uint64_t head[8];
+    int pos[8];
 #pragma unroll
-    for (int l = 0; l < SM; ++l) {
-      pos[l] = ((asc >> l) & 1u) ? k - 1 : 0;
-      head[l] = l < num_lists ? mine[l * lstride + pos[l]] : 0ull;
+    for (int i = 0; i < 8; ++i) {
+      const int l = r + 4 * i;
+      pos[i] = ((asc >> i) & 1u) ? k - 1 : 0;
+      head[i] = (row_ok && l < num_lists) ? mine[l * lstride + pos[i]] : 0ull;
     }
     for (int o = 0; o < k; ++o) {
       uint64_t best = head[0];
 #pragma unroll
-      for (int l = 1; l < SM; ++l) best = head[l] > best ? head[l] : best;
-      merge_write(best, q, o, k, kind, qn, scale, out_keys, ids, dist);
+      for (int i = 1; i < 8; ++i) best = head[i] > best ? head[i] : best;
 #pragma unroll
-      for (int l = 0; l < SM; ++l) {
-        if (best != 0 && head[l] == best) {
-          const bool up = (asc >> l) & 1u;
-          pos[l] += up ? -1 : 1;
-          head[l] = (pos[l] >= 0 && pos[l] < k) ? mine[l * lstride + pos[l]] : 0ull;
+      for (int off = 1; off <= 2; off <<= 1) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, best, off);
+        best = other > best ? other : best;
+      }
+      if (r == 0 && row_ok) merge_write(best, q, o, k, kind, qn, scale, out_keys, ids, dist);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (best != 0 && head[i] == best) {
+          const int l = r + 4 * i;
+          pos[i] += ((asc >> i) & 1u) ? -1 : 1;
+          head[i] = (pos[i] >= 0 && pos[i] < k) ? mine[l * lstride + pos[i]] : 0ull;
         }
       }
     }
     return;
   }
 
+  if (r != 0 || !row_ok) return;
   // ascending: key[0] the worst kept (0 while fewer than k are held); slots
   // k .. KR-1 hold ~0 and never change
   uint64_t key[KR];

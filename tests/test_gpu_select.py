@@ -102,14 +102,15 @@ def test_refine_device_missing_and_errors():
 @pytest.mark.parametrize("order", ["random", "best_first", "worst_first", "mixed"])
 @pytest.mark.parametrize("k,lists,nq", [(1, 7, 45), (4, 30, 100), (5, 2, 33), (10, 13, 10_000),
                                         (10, 19, 77), (10, 20, 70), (16, 12, 64), (17, 5, 31),
-                                        (32, 6, 50), (32, 7, 40), (1, 40, 64)])
+                                        (32, 6, 50), (32, 7, 40), (32, 24, 20), (1, 40, 64),
+                                        (10, 40, 50)])
 def test_merge_keys_duplicates_and_empty_slots(k, lists, nq, order):
     # the candidate lists of the units or ranks of one search: a key may sit
     # in several lists (units start from an earlier unit's list), slots may
     # be empty (0); lists come best first (merged lists), worst first with
     # the empty slots in front (the fused kernel's register lists) or in no
-    # order (its heaps).  Up to 192 candidates in up to 32 lists per query
-    # take the lane-per-query merge, more the warp-per-query one.
+    # order (its heaps).  Up to 768 candidates in up to 32 lists per query
+    # take the four-lanes-per-query merge, more lists the warp-per-query one.
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(1000 * k + lists)
     table = rng.integers(-40, 40, size=(nq, 300)).astype(np.float32)
