@@ -253,16 +253,18 @@ void launch_prep(const PrepParams& p, int sms, cudaStream_t s) {
 
 void launch_merge(const uint64_t* lists, int num_lists, int64_t list_rows, int64_t nq, int k,
                   int kind, const float* qq, uint64_t* out_keys, int32_t* ids, float* dist,
-                  cudaStream_t s, float scale = 1.0f) {
+                  cudaStream_t s, float scale = 1.0f, const float* queries = nullptr,
+                  int d = 0) {
   if (nq == 0) return;
   int64_t total = (int64_t)num_lists * k;
-  if (k <= 32 && total <= MERGE_QUAD_MAX && num_lists <= 32) {
+  if (merge_quad_fits(num_lists, k)) {
     ProfScope prof("merge", s);
     const unsigned blocks = (unsigned)((nq + 7) / 8);
     const size_t smem = (size_t)total * 8 * sizeof(uint64_t);
 #define MLXVS_MERGE_QUAD(KR_)                                                              \
   merge_keys_quad_kernel<KR_><<<blocks, 32, smem, s>>>(lists, num_lists, list_rows, nq, k, \
-                                                         kind, qq, out_keys, ids, dist, scale)
+                                                         kind, qq, out_keys, ids, dist, scale, \
+                                                         queries, d)
     if (k <= 10)
       MLXVS_MERGE_QUAD(10);
     else if (k <= 16)
@@ -1262,9 +1264,13 @@ void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kin
   require(lists != nullptr || num_lists == 0, "[mlxvs::merge_keys] lists must not be NULL.");
   Scratch sc(s);
   float* qq = nullptr;
+  // the four-lanes merge computes |q|^2 itself; the others read it from qq
+  const bool quad = merge_quad_fits(num_lists, k);
   if (kind == static_cast<int>(Metric::L2)) {
     require(queries != nullptr && d >= 1,
             "[mlxvs::merge_keys] L2 distances need the queries [nq, d].");
+  }
+  if (kind == static_cast<int>(Metric::L2) && !quad) {
     qq = sc.alloc<float>((size_t)nq);
     unsigned blocks = (unsigned)std::min<int64_t>((nq + 7) / 8, (int64_t)dev.sms * 16);
     ProfScope prof("sumsq", s);
@@ -1275,7 +1281,8 @@ void merge_keys(const uint64_t* lists, int num_lists, int64_t nq, int k, int kin
     launch_fill(nq * k, kind, ids, dist, nullptr, s);
     return;
   }
-  launch_merge(lists, num_lists, nq, nq, k, kind, qq, nullptr, ids, dist, s);
+  launch_merge(lists, num_lists, nq, nq, k, kind, qq, nullptr, ids, dist, s, 1.0f,
+               quad ? queries : nullptr, d);
 }
 
 void device_synchronize(cudaStream_t s) {

@@ -584,6 +584,11 @@ __device__ __forceinline__ void merge_write(uint64_t key, int64_t q, int o, int 
   }
 }
 
+// Whether merge_keys_quad_kernel takes a merge of num_lists lists of k keys.
+__host__ __device__ inline bool merge_quad_fits(int64_t num_lists, int k) {
+  return k <= 32 && num_lists <= 32 && num_lists * k <= MERGE_QUAD_MAX;
+}
+
 // The same merge with four lanes per query (eight queries per warp), for
 // k <= KR <= 32, at most 32 lists and at most MERGE_QUAD_MAX candidates per
 // query.  The warp copies its queries' rows of every list into shared
@@ -596,13 +601,16 @@ __device__ __forceinline__ void merge_write(uint64_t key, int64_t q, int o, int 
 // then over the four lanes by two shuffles), and every head equal to it
 // moves on (a key present in two lists is taken once).  Otherwise the first
 // lane of each query keeps its k best in a sorted register list
-// (list_insert), skipping a key it already holds.
+// (list_insert), skipping a key it already holds.  For L2 distances the
+// kernel takes |q|^2 from qq, or computes it from queries [nq, d] when qq is
+// null.
 template <int KR>
 __global__ void __launch_bounds__(32)
     merge_keys_quad_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
                            int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
                            const float* __restrict__ qq, uint64_t* __restrict__ out_keys,
-                           int32_t* __restrict__ ids, float* __restrict__ dist, float scale) {
+                           int32_t* __restrict__ ids, float* __restrict__ dist, float scale,
+                           const float* __restrict__ queries, int32_t d) {
   extern __shared__ __align__(16) uint64_t stage[];  // [num_lists][8][k]
   const int lane = threadIdx.x;
   const int64_t q0 = (int64_t)blockIdx.x * 8;
@@ -615,6 +623,28 @@ __global__ void __launch_bounds__(32)
       asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst + 8u * (uint32_t)i),
                    "l"(src + i)
                    : "memory");
+  }
+  // L2 without qq: |q|^2 of the warp's queries [nq, d] while the copies
+  // land, in row_sumsq_kernel's order (lane-strided sums, then warp_sum)
+  float qn_rows = 0.0f;
+  if (kind == 1 && qq == nullptr && queries != nullptr) {
+    float ssq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ssq[i] = 0.0f;
+    for (int c = lane; c < d; c += 32) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < rows) {
+          const float v = __ldg(queries + (size_t)(q0 + i) * d + c);
+          ssq[i] += v * v;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float t = warp_sum(ssq[i]);
+      if ((lane >> 2) == i) qn_rows = t;
+    }
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncwarp();
@@ -645,7 +675,7 @@ __global__ void __launch_bounds__(32)
       sorted = up || down;
     }
   }
-  const float qn = (kind == 1 && qq && row_ok) ? qq[q] : 0.0f;
+  const float qn = (kind == 1 && row_ok) ? (qq ? qq[q] : qn_rows) : 0.0f;
 
   if (__all_sync(0xffffffffu, sorted)) {
     uint64_t head[8];

@@ -142,3 +142,26 @@ def test_merge_keys_duplicates_and_empty_slots(k, lists, nq, order):
     gids, gdist = mv.merge_keys(t, k, "inner_product")
     assert np.array_equal(gids.cpu().numpy(), oids)
     assert np.array_equal(gdist.cpu().numpy(), oscores)
+
+
+@pytest.mark.parametrize("lists", [6, 40])
+def test_merge_keys_l2_distances(lists):
+    # L2 distances max(|q|^2 - score, 0) of merged keys: up to 32 lists the
+    # merge kernel computes |q|^2 itself, past that a separate pass does
+    torch = pytest.importorskip("torch")
+    k, nq, d = 10, 1000, 37
+    rng = np.random.default_rng(lists)
+    q = rng.integers(0, 256, size=(nq, d)).astype(np.float32)
+    ids = np.argsort(rng.random((lists, nq, 500)), axis=2)[..., :k]
+    scores = rng.integers(0, 2 ** 20, size=(lists, nq, k)).astype(np.float32)
+    keys = (O._order_bits(scores).astype(np.uint64) << np.uint64(32)) | \
+        (~ids.astype(np.uint32)).astype(np.uint64)
+    keys = np.sort(keys, axis=2)[..., ::-1].copy()
+    best = np.sort(keys.transpose(1, 0, 2).reshape(nq, -1), axis=1)[:, ::-1][:, :k]
+    oids, oscores = O.decode_keys(best)
+    qn = (q.astype(np.float64) ** 2).sum(1).astype(np.float32)  # exact: integers < 2^24
+    odist = np.maximum(qn[:, None] - oscores, 0).astype(np.float32)
+    t = torch.from_numpy(keys.view(np.int64)).cuda()
+    gids, gdist = mv.merge_keys(t, k, "l2", torch.from_numpy(q).cuda())
+    assert np.array_equal(gids.cpu().numpy(), oids)
+    assert np.array_equal(gdist.cpu().numpy(), odist)
