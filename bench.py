@@ -541,6 +541,13 @@ def main():
     if kern_launches > 0:
         per_launch_s = kern_ms / kern_launches / 1e3
         n_local = hi - lo
+        # the committed captures are single-GPU runs; a rank's kernel works
+        # through its share of the base rows (or of the rows to list), so
+        # its DRAM bytes are scaled by that share
+        share = (hi - lo) / w["n"]
+        traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.workload)
+        if traffic is not None and world > 1:
+            traffic *= share
         if is_hamming and kname == "hamming_mma":
             # codes as +-1 int8 on the tensor cores: 2 * Q * N * bits integer
             # ops per launch, against twice the measured bf16 rate (int8 runs
@@ -552,7 +559,8 @@ def main():
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
                     "frac": ach / peak, "issued_frac": issued_ops / kern_launches
                     / per_launch_s / 1e12 / peak,
-                    "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
+                    "traffic": traffic,
+                    "traffic_source": "ncu capture of one GPU" + (f", scaled by this rank's share {share:.3f}" if world > 1 else ""),
                     "peak_source": f"2 x {peaks['source']} bf16 sustained",
                     "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"2*Q*N*bits = {ops:.3e} int8 ops "
@@ -579,7 +587,8 @@ def main():
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                     "frac": ach / peak, "issued_frac": issued_ops / kern_launches
                     / per_launch_s / 1e12 / peak,
-                    "traffic": NCU_TRAFFIC_PER_LAUNCH.get(args.workload),
+                    "traffic": traffic,
+                    "traffic_source": "ncu capture of one GPU" + (f", scaled by this rank's share {share:.3f}" if world > 1 else ""),
                     "peak_source": f"{peaks['source']} bf16 sustained (the kernel runs back to "
                                    f"back for the whole timed region)",
                     "frac_of_burst": ach / peaks["bf16"], "kernel": kname,
