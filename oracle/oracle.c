@@ -322,6 +322,9 @@ int oracle_hamming_knn(const uint8_t* rows, int64_t n, const uint8_t* queries,
   return 0;
 }
 
+/* The best k distinct keys of L lists per query, best first (0 = empty):
+ * a key that sits in several lists (the GPU search's units start from an
+ * earlier unit's list) is taken once. */
 void oracle_merge_keys(const uint64_t* lists, int32_t L, int64_t nq, int32_t k,
                        uint64_t* out) {
 #pragma omp parallel for schedule(static)
@@ -330,7 +333,10 @@ void oracle_merge_keys(const uint64_t* lists, int32_t L, int64_t nq, int32_t k,
     for (int32_t l = 0; l < L; ++l)
       for (int32_t j = 0; j < k; ++j) {
         uint64_t key = lists[((size_t)l * nq + i) * k + j];
-        if (key > h[0]) heap_push(h, k, key);
+        if (key <= h[0]) continue;
+        int held = 0;
+        for (int32_t s = 0; s < k && !held; ++s) held = h[s] == key;
+        if (!held) heap_push(h, k, key);
       }
     qsort(h, (size_t)k, sizeof(uint64_t), cmp_desc);
     memcpy(out + (size_t)i * k, h, (size_t)k * sizeof(uint64_t));

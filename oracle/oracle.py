@@ -111,7 +111,8 @@ def hamming_knn(rows, queries, k, threads=0):
 
 
 def merge_keys(lists, k):
-    """Best k of L key lists laid out [L, nq, k] (0 = empty slot)."""
+    """Best k distinct keys of L key lists laid out [L, nq, k] (0 = empty
+    slot), best first; a key present in several lists is taken once."""
     lib = _load()
     lists = np.ascontiguousarray(lists, dtype=np.uint64)
     L, nq, kk = lists.shape

@@ -89,6 +89,23 @@ def test_merge_keys_is_global_topk():
     assert (merged == full).all()
 
 
+def test_merge_keys_takes_repeated_keys_once():
+    # lists sharing keys (the GPU search's units start from an earlier
+    # unit's list), in any order, with empty slots
+    rng = np.random.default_rng(5)
+    L, nq, k = 9, 40, 10
+    ids = rng.integers(0, 60, size=(L, nq, k))
+    table = rng.integers(-20, 20, size=(nq, 60)).astype(np.float32)
+    scores = np.take_along_axis(table[None].repeat(L, 0), ids, axis=2)
+    keys = np.vectorize(lambda s, i: O.key(float(s), int(i)), otypes=[np.uint64])(scores, ids)
+    keys[rng.random(keys.shape) < 0.2] = 0
+    merged = O.merge_keys(keys, k)
+    for i in range(nq):
+        u = np.unique(keys[:, i, :])[::-1]
+        u = u[u != 0][:k]
+        assert (merged[i, :len(u)] == u).all() and (merged[i, len(u):] == 0).all()
+
+
 def test_key_order():
     # higher score first, then lower id (src/kernels.h:20-23)
     assert O.key(2.0, 5) > O.key(1.0, 0)
