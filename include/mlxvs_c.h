@@ -287,8 +287,10 @@ MLXVS_C_API int mlxvs_hamming_keys_device(
     void* stream);
 
 /**
- * Merges num_lists key lists laid out [num_lists][nq][k] into the k best per
- * query (ties keep the lower id) and converts them to ids and distances of
+ * Merges num_lists key lists laid out [num_lists][nq][k] into the k best
+ * distinct keys per query (ties keep the lower id; a key present in several
+ * lists is taken once; the lists may come in any order, sorted ones merge
+ * fastest) and converts them to ids and distances of
  * the given kind (an mlxvs_metric, or MLXVS_KIND_HAMMING).  For MLXVS_L2 the
  * distance is max(|q|^2 - score, 0) (ref: src/knn.cpp:122-131), so queries
  * [nq, d] must be given; otherwise queries may be NULL.
