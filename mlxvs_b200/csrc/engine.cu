@@ -700,6 +700,12 @@ struct FusedPlan {
   uint32_t smem;
 };
 
+// The start cost of a unit in tiles, for choose_splits (a compile-time
+// constant so that other values can be built and timed).
+#ifndef MLXVS_UNIT_OVERHEAD_TILES
+#define MLXVS_UNIT_OVERHEAD_TILES 3.0
+#endif
+
 FusedPlan plan_fused(const DeviceInfo& dev, int npa, bool fold, int nbm, int kchunks, int k,
                      int64_t nq, int64_t n_pad, int64_t nq_pad, int d_pad, const __half* q_hi,
                      const __half* q_lo, const __half* b_hi, const __half* b_lo,
@@ -710,7 +716,7 @@ FusedPlan plan_fused(const DeviceInfo& dev, int npa, bool fold, int nbm, int kch
   const int QB = f.shape.qb;
   const int qblocks = (int)((nq + QB - 1) / QB);
   const int tiles = (int)(n_pad / GT_BN);
-  const int splits = choose_splits(qblocks, tiles, dev.sms, 3.0, 64);
+  const int splits = choose_splits(qblocks, tiles, dev.sms, MLXVS_UNIT_OVERHEAD_TILES, 64);
   const int units = qblocks * splits;
 
   f.partial = sc.alloc<uint64_t>((size_t)splits * nq_pad * k);
