@@ -1,36 +1,36 @@
-"""cuVS's ``cuvs.neighbors.brute_force`` (build, search, save, load) over the
-sm_100a exact search of this library.
+"""The search half of cuVS's ``cuvs.neighbors.brute_force`` API (``build``
+and ``search``), routed to this library's sm_100a exact search.
 
-Follows python/mlxvs/cuvs/neighbors/brute_force.py:14-190.  The metrics the
-GPU search computes run there: ``sqeuclidean``, ``euclidean``/``l2``,
-``inner_product`` and ``cosine`` through :func:`mlxvs_b200.brute_force_knn`,
-and ``bitwise_hamming`` (bit-packed uint8 rows) through
-:func:`mlxvs_b200.hamming_knn` -- the re-pointed branches of
-brute_force.py:98-116.  The elementwise metrics (l1, chebyshev, canberra, ...)
-and prefilters, which the reference computes with a dense pairwise matrix,
-are not part of this library: :func:`search` raises NotImplementedError for
-them rather than computing anything on the host.
+It stands in for the branches of python/mlxvs/cuvs/neighbors/brute_force.py:98-116
+that call the reference's ``brute_force_knn`` and ``hamming_knn``.  Metric
+routing:
 
-Placement: when the dataset or the queries is a CUDA tensor the search runs
-on that GPU (the dataset's, when both are) and returns CUDA tensors;
-otherwise it goes through the host entry and returns numpy arrays.
+* ``sqeuclidean``, ``euclidean``/``l2``, ``inner_product`` and ``cosine`` go to
+  :func:`mlxvs_b200.brute_force_knn`, whose scores are then turned into cuVS
+  distances;
+* ``bitwise_hamming`` (rows of bit-packed uint8) goes to
+  :func:`mlxvs_b200.hamming_knn`;
+* every other cuVS metric, and any real prefilter, raises NotImplementedError:
+  the library has no kernel for them and computes nothing on the host.
+
+Index files (cuVS ``save``/``load``) are not part of this library.
+
+Where the work runs: on the GPU of the dataset when it is a CUDA tensor (else
+of the queries, when they are), returning CUDA tensors; for host inputs,
+through the host-memory entry, returning numpy arrays.
 """
 
 import numpy as np
 
 import mlxvs_b200 as _mv
-from mlxvs_b200.cuvs import _records as rec
 from mlxvs_b200.cuvs import distance as _d
 
-__all__ = ["Index", "build", "load", "save", "search"]
-
-SERIALIZATION_VERSION = 0
-# format version whose half-precision dtype prefix the file uses
-_PREFIX_VERSION = 6
+__all__ = ["Index", "build", "search"]
 
 
 class Index:
-    """A brute-force index: the dataset and its metric."""
+    """What ``build`` returns: a reference to the rows plus the metric to
+    search them with."""
 
     def __init__(self):
         self.trained = False
@@ -100,17 +100,19 @@ def _out(array, given):
 
 
 def build(dataset, metric="sqeuclidean", metric_arg=2.0, resources=None):
-    """Builds the index of the dataset (it keeps the rows), as cuVS's
-    ``brute_force.build``.
+    """Wraps ``dataset`` as an index for :func:`search`; nothing is computed
+    (an exact search needs no structure beyond the rows).
 
     Args:
-        dataset: Rows ``[n, dim]`` (a CUDA tensor stays on its GPU), float
-          for the float metrics, bit-packed uint8 for ``"bitwise_hamming"``.
-        metric (str | int): A name of ``cuvs.distance.DISTANCE_TYPES`` or a
+        dataset: ``[n, dim]`` rows.  Float rows for the float metrics,
+          bit-packed uint8 rows for ``"bitwise_hamming"``.  A CUDA tensor is
+          kept on its device; other inputs are kept as numpy arrays.
+        metric (str | int): a metric name from ``cuvs.distance`` or its
           DistanceType number.
-        metric_arg (float): ``p`` of ``"minkowski"`` (kept for the file).
-        resources: Accepted for compatibility; the search runs on the
-          current CUDA stream of the dataset's device.
+        metric_arg (float): kept on the index (only ``"minkowski"`` uses it,
+          and that metric is not searched here).
+        resources: ignored; the work is queued on the current CUDA stream of
+          the device that holds the rows.
 
     Returns:
         Index
@@ -127,22 +129,23 @@ def build(dataset, metric="sqeuclidean", metric_arg=2.0, resources=None):
 
 
 def search(index, queries, k, neighbors=None, distances=None, resources=None, prefilter=None):
-    """The k nearest rows of every query, as cuVS's ``brute_force.search``.
+    """Exact k nearest neighbors of each query row among the index rows.
 
     Args:
-        index (Index): Built by :func:`build` or read by :func:`load`.
-        queries: Rows ``[n_queries, dim]`` of the dataset's kind.
-        k (int): Neighbors per query, 1 to 256; beyond the dataset's rows the
-          lists are padded with id -1 and an infinite distance (minus
-          infinity for the inner product).
-        neighbors: Optional ``int64 [n_queries, k]`` output, written in place.
-        distances: Optional ``float32 [n_queries, k]`` output, written in place.
-        resources: Accepted for compatibility.
-        prefilter: Only None or a filter of type ``"none"``.
+        index (Index): from :func:`build`.
+        queries: ``[n_queries, dim]`` rows of the same kind as the dataset.
+        k (int): 1 .. 256.  Slots past the number of rows hold id -1 and an
+          infinite distance (negative infinity for ``inner_product``).
+        neighbors: optional preallocated ``[n_queries, k]`` array or tensor
+          that receives the ids.
+        distances: optional preallocated ``[n_queries, k]`` array or tensor
+          that receives the distances.
+        resources: ignored.
+        prefilter: None, or a filter whose ``type`` is ``"none"``.
 
     Returns:
-        tuple: ``(distances, neighbors)``, nearest first, ties to the lower
-        id; float32 and int64.
+        tuple: ``(distances, neighbors)`` as float32 and int64, each row in
+        increasing distance, equal distances ordered by row id.
     """
     if not index.trained:
         raise ValueError("Index needs to be built before calling search.")
@@ -173,56 +176,3 @@ def search(index, queries, k, neighbors=None, distances=None, resources=None, pr
         dist = dist.astype(np.float32, copy=False)
     return _out(dist, distances), _out(ids, neighbors)
 
-
-def save(filename, index, include_dataset=True, resources=None):
-    """Saves the index in cuVS's brute-force format (version 0): the dataset's
-    dtype prefix, then as NumPy records the version, rows, dim, metric,
-    metric_arg, whether the dataset follows, the dataset, whether norms
-    follow and the row norms (squared for L2, plain for cosine)."""
-    data = np.ascontiguousarray(_host(index._dataset))
-    t = index._metric
-    with open(filename, "wb") as f:
-        f.write(rec.dtype_prefix(data.dtype, _PREFIX_VERSION))
-        rec.write_scalar(f, SERIALIZATION_VERSION, np.int32)
-        rec.write_scalar(f, data.shape[0], np.uint64)
-        rec.write_scalar(f, data.shape[1], np.uint64)
-        rec.write_scalar(f, t, np.int32)
-        rec.write_scalar(f, index._metric_arg, np.float32)
-        rec.write_scalar(f, bool(include_dataset), np.bool_)
-        if include_dataset:
-            rec.write_array(f, data)
-        has_norms = t in (_d.L2Expanded, _d.L2SqrtExpanded, _d.CosineExpanded)
-        rec.write_scalar(f, has_norms, np.bool_)
-        if has_norms:
-            x = data.astype(np.float32)
-            norms = np.sum(x * x, axis=1)
-            if t == _d.CosineExpanded:
-                norms = np.sqrt(norms)
-            rec.write_array(f, norms.astype(np.float32))
-
-
-def load(filename, resources=None):
-    """Loads a brute-force index saved by :func:`save` or by cuVS; the dataset
-    is a host array (search copies it to the GPU on every call; build an
-    index of a CUDA tensor of it to keep it resident)."""
-    with open(filename, "rb") as f:
-        dtype = rec.read_prefix(f)
-        ver = rec.read_scalar(f)
-        if ver != SERIALIZATION_VERSION:
-            raise ValueError(
-                f"serialization version mismatch, expected {SERIALIZATION_VERSION}, got {ver}")
-        rows = rec.read_scalar(f)
-        dim = rec.read_scalar(f)
-        metric = rec.read_scalar(f)
-        metric_arg = rec.read_scalar(f)
-        if not rec.read_scalar(f):
-            raise ValueError("the file holds no dataset; brute force needs it")
-        data = rec.read_array(f).astype(dtype, copy=False)
-    if data.shape != (rows, dim):
-        raise ValueError(f"dataset of shape {data.shape}, the file says ({rows}, {dim})")
-    idx = Index()
-    idx._dataset = np.ascontiguousarray(data)
-    idx._metric = int(metric)
-    idx._metric_arg = float(metric_arg)
-    idx.trained = True
-    return idx

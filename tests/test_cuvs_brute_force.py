@@ -2,16 +2,10 @@
 (python/mlxvs/cuvs/neighbors/brute_force.py; its tests
 python/tests/test_cuvs.py:147-221,777-793).
 
-CPU: the index file (every record a valid .npy record that numpy's own
-reader parses), the metric table, the distance conversion and the refusals.
+CPU: the metric table, the distance conversion and the refusals.
 GPU: searches through the sm_100a kernels, bit-exact against the oracle on
 integer data for the L2 and inner-product metrics and on Hamming codes,
-recall 1 for cosine, host and CUDA inputs, outputs written in place, a saved
-and loaded index searching the same."""
-
-import ast
-import io
-import struct
+recall 1 for cosine, host and CUDA inputs, outputs written in place."""
 
 import numpy as np
 import pytest
@@ -22,84 +16,6 @@ from oracle import oracle as O
 from tests import data
 
 FAST_METRICS = ["sqeuclidean", "euclidean", "l2", "inner_product", "cosine"]
-
-
-def _records(raw):
-    """The dtype prefix and every .npy record of an index file.  Records are
-    parsed with numpy's own format reader, except float16 data, which the
-    format writes with RAFT's dtype string "<e2" that numpy does not read."""
-    f = io.BytesIO(raw[4:])
-    out = []
-    while f.tell() < len(raw) - 4:
-        start = f.tell()
-        assert np.lib.format.read_magic(f) == (1, 0)
-        (size,) = struct.unpack("<H", f.read(2))
-        header = f.read(size)
-        assert header.endswith(b"\n") and (f.tell() - start) % 64 == 0  # padded to 64
-        fields = ast.literal_eval(header.decode("latin1"))
-        assert set(fields) == {"descr", "fortran_order", "shape"}
-        assert not fields["fortran_order"]
-        if fields["descr"] == "<e2":
-            dtype, shape = np.dtype(np.float16), fields["shape"]
-        else:
-            f.seek(start + 8)
-            shape, _, dtype = np.lib.format.read_array_header_1_0(f)
-        count = int(np.prod(shape)) if shape else 1
-        a = np.frombuffer(f.read(count * dtype.itemsize), dtype=dtype).reshape(shape)
-        out.append(a)
-    return raw[:4], out
-
-
-def test_file_layout_cosine(tmp_path):
-    # python/tests/test_cuvs.py:214-221, and every record read back
-    x = np.random.default_rng(5).random((10, 3)).astype(np.float32)
-    path = tmp_path / "bf.bin"
-    bf.save(str(path), bf.build(x, "cosine"))
-    raw = path.read_bytes()
-    assert raw[:4] == b"<f4\0"
-    assert raw[4:10] == b"\x93NUMPY"
-    prefix, rec = _records(raw)
-    assert [r.dtype for r in rec[:6]] == [np.int32, np.uint64, np.uint64, np.int32,
-                                          np.float32, np.uint8]
-    assert rec[0][()] == 0 and rec[1][()] == 10 and rec[2][()] == 3
-    assert rec[3][()] == D.CosineExpanded and rec[4][()] == np.float32(2.0)
-    assert rec[5][()] == 1
-    assert np.array_equal(rec[6], x)
-    assert rec[7][()] == 1
-    assert np.array_equal(rec[8], np.sqrt(np.sum(x * x, axis=1)))
-    assert len(rec) == 9
-
-
-@pytest.mark.parametrize("metric,dtype,norms", [
-    ("sqeuclidean", np.float32, True), ("euclidean", np.float16, True),
-    ("inner_product", np.float32, False), ("bitwise_hamming", np.uint8, False)])
-def test_save_load_roundtrip(tmp_path, metric, dtype, norms):
-    rng = np.random.default_rng(6)
-    x = (rng.integers(0, 256, (37, 16)) if dtype == np.uint8 else rng.random((37, 16)))
-    x = x.astype(dtype)
-    path = str(tmp_path / "i.bin")
-    bf.save(path, bf.build(x, metric, metric_arg=3.0))
-    raw = open(path, "rb").read()
-    prefix, rec = _records(raw)
-    assert prefix == {np.float32: b"<f4\0", np.float16: b"<f2\0", np.uint8: b"|u1\0"}[dtype]
-    assert rec[7][()] == int(norms) and len(rec) == (9 if norms else 8)
-    idx = bf.load(path)
-    assert idx.trained and len(idx) == 37 and idx.metric == metric
-    assert idx._metric_arg == 3.0
-    assert idx.dataset.dtype == dtype and np.array_equal(idx.dataset, x)
-
-
-def test_load_refusals(tmp_path):
-    x = np.zeros((4, 2), np.float32)
-    path = str(tmp_path / "n.bin")
-    bf.save(path, bf.build(x), include_dataset=False)
-    with pytest.raises(ValueError, match="no dataset"):
-        bf.load(path)
-    bad = tmp_path / "v.bin"
-    raw = bytearray(open(path, "rb").read())
-    bad.write_bytes(bytes(raw[:4]) + b"junk")
-    with pytest.raises(ValueError):
-        bf.load(str(bad))
 
 
 def test_metric_table():
@@ -173,8 +89,7 @@ def test_integer_rows_bit_exact(metric, where):
 @pytest.mark.gpu
 @pytest.mark.parametrize("metric", FAST_METRICS)
 @pytest.mark.parametrize("inplace", [True, False])
-@pytest.mark.parametrize("serialize", [True, False])
-def test_uniform_rows_as_reference(metric, inplace, serialize, tmp_path):
+def test_uniform_rows_as_reference(metric, inplace):
     # python/tests/test_cuvs.py:162-194 for the metrics the GPU search runs
     rng = np.random.default_rng(3)
     index = rng.random((100, 40)).astype(np.float32)
@@ -183,10 +98,6 @@ def test_uniform_rows_as_reference(metric, inplace, serialize, tmp_path):
     indices = np.zeros((32, k), np.int64)
     distances = np.zeros((32, k), np.float32)
     idx = bf.build(index, metric)
-    if serialize:
-        path = str(tmp_path / "bf.bin")
-        bf.save(path, idx)
-        idx = bf.load(path)
     ret_d, ret_i = bf.search(idx, queries, k, neighbors=indices if inplace else None,
                              distances=distances if inplace else None)
     got = (distances if inplace else ret_d).copy()
@@ -252,16 +163,14 @@ def _hamming(a, b):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bytes_", [3, 16, 128])
-def test_bitwise_hamming_as_reference(bytes_, tmp_path):
+def test_bitwise_hamming_as_reference(bytes_):
     # python/tests/test_cuvs.py:777-793 without the prefilter, and bit-exact
     # against the oracle (ties to the lower id)
     rng = np.random.default_rng(11)
     codes = rng.integers(0, 256, (700, bytes_), dtype=np.uint8)
     queries = rng.integers(0, 256, (40, bytes_), dtype=np.uint8)
     index = bf.build(codes, metric="bitwise_hamming")
-    path = str(tmp_path / "h.bin")
-    bf.save(path, index)
-    d, i = bf.search(bf.load(path), queries, 7)
+    d, i = bf.search(index, queries, 7)
     want = np.sort(_hamming(queries, codes), axis=1)[:, :7]
     np.testing.assert_array_equal(d, want)
     np.testing.assert_array_equal(np.take_along_axis(_hamming(queries, codes), i, 1), want)
