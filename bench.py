@@ -79,20 +79,32 @@ DEFAULT_WORKLOAD = "knn-l2-1m-k10"
 FLUSH_BYTES = 256 << 20
 METRIC = "exact k-NN queries/s (1M×128 fp32, k=10) at 1/2/4/8 B200; % tensor-pipe roofline"
 
-# DRAM bytes per launch of the dominant kernel, from the committed ncu
-# summaries under profiles/ (None until captured for that workload).
-NCU_TRAFFIC_PER_LAUNCH = {
-    # profiles/knn_gemm_topk_config1.md: 371.3 MB read + 11.8 MB written
-    "knn-l2-1m-k10": 383.1e6,
-    # profiles/knn_gemm_collect_config2_200k.md: the collecting pass
-    "knn-cos-200k-1536": 992.3e6,
-    # the same scaled by rows to config 2 (5x the base tiles)
-    "knn-cos-1m-1536": 4.962e9,
-    # profiles/knn_gemm_topk_i8_hamming_1m.md: 3.32 GB at 1M codes
-    "hamming-1m-1024b": 3.322e9,
-    # the same, scaled by rows to 10M codes (10x the base tiles)
-    "hamming-10m-1024b": 33.22e9,
-}
+# DRAM bytes per launch of the dominant kernel, measured by ncu for the
+# exact kernel variant and the per-rank work of each world size (a rank's
+# shard emulated on one GPU with --shard-of N): profiles/traffic.json, keyed
+# "workload@N", each entry with the command that produced it.
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "traffic.json")
+
+
+def load_traffic(workload, world):
+    try:
+        with open(TRAFFIC_FILE) as f:
+            table = json.load(f)
+    except (OSError, ValueError):
+        return None, "no capture"
+    e = table.get(f"{workload}@{world}")
+    if not e:
+        return None, f"no capture of {workload} at N={world}"
+    return e["bytes_per_launch"], e.get("source", "ncu")
+
+
+def host_threads():
+    """Host cores this process may run on (torchrun's OMP_NUM_THREADS=1 does
+    not apply: the oracle is always given this count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
 def env_int(name, default):
@@ -256,6 +268,20 @@ class ClockSampler:
                 "samples": len(loaded), "power_w_max": max_power}
 
 
+def config_of(args, w, world):
+    """The line's config, identical in both arms."""
+    is_allnn = w["kind"] == "allnn"
+    cfg = {"workload": args.workload, "desc": w["desc"], "n": w["n"], "queries": w["nq"],
+           "k": w["k"],
+           "parallelism": (f"rows to list split over {world} GPU(s), all rows on each"
+                           if is_allnn else f"base rows sharded over {world} GPU(s)"),
+           "l2_flush": f"{FLUSH_BYTES >> 20} MiB buffer written before every timed step "
+                       f"(outside the per-step event spans)"}
+    if getattr(args, "shard_of", 1) > 1:
+        cfg["shard_of"] = args.shard_of
+    return cfg
+
+
 # ---------------------------------------------------------------- CPU side
 
 def cpu_sample_rate(w, base_np, q_np, budget_s, threads=0):
@@ -292,22 +318,22 @@ def reference_arm(args, w, peaks):
         return 0
     import torch
 
-    cores = os.cpu_count() or 1
+    cores = host_threads()
     base, q = make_inputs(w, "cpu")
     base_np, q_np = base.numpy(), q.numpy()
     # each step: a bounded sample of the workload (all base rows, the first
     # m queries), m chosen so the whole run stays within a few minutes
     per_step = max(0.05, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
-    rate, m, _ = cpu_sample_rate(w, base_np, q_np, per_step)
+    rate, m, _ = cpu_sample_rate(w, base_np, q_np, per_step, threads=cores)
     from oracle import oracle as O
 
     def step():
         if w["kind"] == "hamming":
-            O.hamming_knn(base_np, q_np[:m], w["k"])
+            O.hamming_knn(base_np, q_np[:m], w["k"], threads=cores)
         elif w["kind"] == "allnn":
-            O.all_neighbors(base_np, w["k"], w["metric"], begin=0, end=m)
+            O.all_neighbors(base_np, w["k"], w["metric"], threads=cores, begin=0, end=m)
         else:
-            O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"])
+            O.brute_force_knn(base_np, q_np[:m], w["k"], w["metric"], threads=cores)
 
     for _ in range(args.warmup):
         step()
@@ -325,9 +351,10 @@ def reference_arm(args, w, peaks):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": w["desc"]},
+        "config": config_of(args, w, env_int("WORLD_SIZE", args.gpus)),
         "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "threads": cores,
+                         "omp_num_threads_env": os.environ.get("OMP_NUM_THREADS")},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "the reference (MLX + Metal, macOS only) cannot run here; its CPU "
@@ -335,6 +362,55 @@ def reference_arm(args, w, peaks):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------- parity
+
+PARITY_SAMPLE = {"knn-unit": 200, "allnn": 2_000, "hamming": 500}
+
+
+def check_parity(w, base, q, ids, dist, k, metric):
+    """The last timed step's ids and distances against the oracle on every
+    host thread.  Integer-valued L2 data (configs 0 and 1): every query,
+    bit-exact.  Hamming: a sample of the queries, bit-exact.  all_neighbors:
+    a sample of the rows to list, bit-exact.  Unit rows (config 2): a sample
+    of the queries, distances within rtol = atol = 1e-4 of the oracle's and
+    ids equal wherever the oracle's distances are not tied within that
+    tolerance.  Returns counts of mismatching queries."""
+    from oracle import oracle as O
+
+    threads = host_threads()
+    t0 = time.perf_counter()
+    kind = w["kind"]
+    nq = q.shape[0]
+    m = nq if kind == "knn" else min(nq, PARITY_SAMPLE[kind])
+    gi = ids[:m].cpu().numpy()
+    gd = dist[:m].cpu().numpy()
+    base_np = base.cpu().numpy()
+    if kind == "allnn":
+        oi, od = O.all_neighbors(base_np, k, metric, threads=threads, begin=0, end=m)
+    elif kind == "hamming":
+        oi, od = O.hamming_knn(base_np, q[:m].cpu().numpy(), k, threads=threads)
+    else:
+        oi, od = O.brute_force_knn(base_np, q[:m].cpu().numpy(), k, metric, threads=threads)
+    if kind == "knn-unit":
+        close = np.isclose(gd, od, rtol=1e-4, atol=1e-4)
+        # a position may hold either of two rows whose scores tie within the
+        # tolerance: compare ids only where the oracle's neighbours differ
+        gap = np.abs(np.diff(od, axis=1)) > 1e-4 * np.maximum(1.0, np.abs(od[:, 1:]))
+        sep = np.ones_like(od, dtype=bool)
+        sep[:, 1:] &= gap
+        sep[:, :-1] &= gap
+        bad = ~close.all(axis=1) | ((gi != oi) & sep).any(axis=1)
+        rule = "distances within rtol = atol = 1e-4, ids equal where not tied"
+    else:
+        bad = ~((gi == oi).all(axis=1) & (gd == od).all(axis=1))
+        rule = "ids and distances bit-exact"
+    what = "rows to list" if kind == "allnn" else "queries"
+    return {"checked": int(m), "of": int(nq), "unit": what,
+            "mismatched": int(bad.sum()), "rule": rule,
+            "against": f"oracle/oracle.c on {threads} host threads",
+            "seconds": round(time.perf_counter() - t0, 2)}
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -350,6 +426,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of oracle work for cpu_baseline (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the post-timing comparison with the oracle")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="one process searching the shard rank 0 holds at N GPUs (for "
+                         "per-rank profiles on one GPU); the line is not a bench value")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
@@ -383,11 +464,15 @@ def main():
     base, q = make_inputs(w, dev)
     bounds = mvd.shard_bounds(w["n"], world)
     lo, hi = bounds[rank], bounds[rank + 1]
+    if world == 1 and args.shard_of > 1:
+        # rank 0's shard (or share of the rows to list) at N = shard_of
+        lo, hi = 0, mvd.shard_bounds(w["n"], args.shard_of)[1]
     is_allnn = w["kind"] == "allnn"
     # all_neighbors splits the rows to list (queries) over the GPUs, each
     # holding all rows; the others split the base rows
     shard = base if is_allnn else base[lo:hi].contiguous()
     full_base = base
+    emulated = world == 1 and args.shard_of > 1
     k = w["k"]
     is_hamming = w["kind"] == "hamming"
     metric = None if is_hamming else w["metric"]
@@ -395,7 +480,7 @@ def main():
 
     def step():
         if is_allnn:
-            if world == 1:
+            if world == 1 and not emulated:
                 return mv.all_neighbors(shard, k, metric, algo="brute_force")
             return mv.all_neighbors_rows(shard, k, metric, begin=lo, end=hi)
         if world == 1:
@@ -458,6 +543,15 @@ def main():
         kname = "gemm_topk (sampled pass) + gemm_collect"
         kern_ms += coll_ms
         kern_launches = coll_launches
+    # device time per step of each of the library's kernels (rank 0's
+    # profiled pass); the rest of the step is the host's part and, for
+    # N > 1, the all-gather
+    step_breakdown = {}
+    for name in ("prep", "gemm_topk", "gemm_topk_skipped", "gemm_collect", "hamming_mma",
+                 "hamming_topk", "select_keys", "rescore", "merge", "fill"):
+        ms, nl = mv.profile_read(name)
+        if nl:
+            step_breakdown[name] = ms / prof_steps
     _, all_launches = mv.profile_read(None)
     # launches of this library's kernels in the timed steps (the same per step)
     all_launches = all_launches * args.steps // max(prof_steps, 1)
@@ -468,22 +562,12 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
 
-    # a quick self-check of the last step's output on a few queries (rank 0)
-    check = None
-    if rank == 0 and is_allnn:
-        from oracle import oracle as O
-
-        oids, odist = O.all_neighbors(full_base.cpu().numpy(), k, metric, begin=0, end=4)
-        check = bool(np.array_equal(ids[:4].cpu().numpy(), oids) and
-                     np.array_equal(dist_out[:4].cpu().numpy(), odist))
-    if rank == 0 and not is_hamming and w["kind"] == "knn":
-        from oracle import oracle as O
-
-        qs = q[:4].cpu().numpy()
-        oids, odist = O.brute_force_knn(full_base.cpu().numpy(), qs, k, metric)
-        check = bool(np.array_equal(ids[:4].cpu().numpy(), oids) and
-                     np.array_equal(dist_out[:4].cpu().numpy(), odist))
-
+    # parity of the last timed step's output with the oracle (rank 0, after
+    # timing): every query for the integer-valued configs, a bounded sample
+    # of the queries (or of the rows to list) for the others
+    parity = None
+    if rank == 0 and not args.no_parity and not emulated:
+        parity = check_parity(w, full_base, q, ids, dist_out, k, metric)
     # e2e: the public API on host (pinned) buffers, copies inside the region
     e2e = None
     if args.e2e_steps > 0:
@@ -511,8 +595,8 @@ def main():
                     i, d_ = mvd.sharded_brute_force_knn(sd, qd, k, metric, id_offset=lo)
                 return i.cpu(), d_.cpu()
         e2e_step()
-        barrier()
         torch.cuda.synchronize()
+        barrier()
         te = time.perf_counter()
         for _ in range(args.e2e_steps):
             e2e_step()
@@ -538,16 +622,11 @@ def main():
 
     # roofline of the dominant kernel (rank 0's launches)
     roof = None
+    step_s = elapsed_ms / args.steps / 1e3
     if kern_launches > 0:
         per_launch_s = kern_ms / kern_launches / 1e3
         n_local = hi - lo
-        # the committed captures are single-GPU runs; a rank's kernel works
-        # through its share of the base rows (or of the rows to list), so
-        # its DRAM bytes are scaled by that share
-        share = (hi - lo) / w["n"]
-        traffic = NCU_TRAFFIC_PER_LAUNCH.get(args.workload)
-        if traffic is not None and world > 1:
-            traffic *= share
+        traffic, traffic_src = load_traffic(args.workload, args.shard_of if emulated else world)
         if is_hamming and kname == "hamming_mma":
             # codes as +-1 int8 on the tensor cores: 2 * Q * N * bits integer
             # ops per launch, against twice the measured bf16 rate (int8 runs
@@ -555,13 +634,14 @@ def main():
             bits = w["bytes"] * 8
             ops = 2.0 * w["nq"] * n_local * bits
             ach = ops / per_launch_s / 1e12
-            peak = 2.0 * peaks["bf16_sustained"]
+            peak = 2.0 * peaks["bf16"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
-                    "frac": ach / peak, "issued_frac": issued_ops / kern_launches
-                    / per_launch_s / 1e12 / peak,
-                    "traffic": traffic,
-                    "traffic_source": "ncu capture of one GPU" + (f", scaled by this rank's share {share:.3f}" if world > 1 else ""),
-                    "peak_source": f"2 x {peaks['source']} bf16 sustained",
+                    "frac": ach / peak,
+                    "frac_of_sustained": ach / (2.0 * peaks["bf16_sustained"]),
+                    "step_frac": ops / step_s / 1e12 / peak,
+                    "issued_frac": issued_ops / kern_launches / per_launch_s / 1e12 / peak,
+                    "traffic": traffic, "traffic_source": traffic_src,
+                    "peak_source": f"2 x {peaks['source']} bf16 burst",
                     "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"2*Q*N*bits = {ops:.3e} int8 ops "
                                               f"({w['nq'] * n_local * (bits // 32):.3e} "
@@ -569,13 +649,15 @@ def main():
                     "issued_per_launch": f"{issued_ops / kern_launches:.3e} int8 ops (padded "
                                          f"query blocks x tiles x K)"}
         elif is_hamming:
-            # integer work: 32-bit popcounts per launch; reported against the
-            # HBM copy bandwidth is meaningless here (compute bound), so the
-            # unit is the popcount rate
+            # the popcount kernel: 32-bit popcounts per launch, and the codes
+            # it reads once per pass over the base against HBM bandwidth
             words = w["bytes"] // 4
             pops = w["nq"] * n_local * words
+            gbs = n_local * w["bytes"] / per_launch_s / 1e9
             roof = {"bound": "int-pipe", "achieved": pops / per_launch_s / 1e12,
-                    "unit": "Tpopc32/s", "peak": None, "frac": None, "traffic": None,
+                    "unit": "Tpopc32/s", "peak": None, "frac": None,
+                    "hbm_gbs_codes_once": gbs, "traffic": traffic,
+                    "traffic_source": traffic_src,
                     "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"{pops:.3e} 32-bit popcounts"}
         else:
@@ -583,31 +665,31 @@ def main():
             if is_allnn:  # this rank's rows against all rows
                 flops = 2.0 * (hi - lo) * w["n"] * w["d"]
             ach = flops / per_launch_s / 1e12
-            peak = peaks["bf16_sustained"]
+            peak = peaks["bf16"]
             roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                    "frac": ach / peak, "issued_frac": issued_ops / kern_launches
-                    / per_launch_s / 1e12 / peak,
-                    "traffic": traffic,
-                    "traffic_source": "ncu capture of one GPU" + (f", scaled by this rank's share {share:.3f}" if world > 1 else ""),
-                    "peak_source": f"{peaks['source']} bf16 sustained (the kernel runs back to "
-                                   f"back for the whole timed region)",
-                    "frac_of_burst": ach / peaks["bf16"], "kernel": kname,
-                    "kernel_ms": per_launch_s * 1e3,
+                    "frac": ach / peak,
+                    "frac_of_sustained": ach / peaks["bf16_sustained"],
+                    "step_frac": flops / step_s / 1e12 / peak,
+                    "issued_frac": issued_ops / kern_launches / per_launch_s / 1e12 / peak,
+                    "traffic": traffic, "traffic_source": traffic_src,
+                    "peak_source": f"{peaks['source']} bf16 burst (dense cuBLAS GEMM)",
+                    "kernel": kname, "kernel_ms": per_launch_s * 1e3,
                     "algorithmic_per_launch": f"2*Q*N*D = {flops:.3e} FLOP",
                     "issued_per_launch": f"{issued_ops / kern_launches:.3e} FLOP (padded query "
                                          f"blocks x tiles x (passes x padded D + 16 for "
                                          f"|b|^2), sampled pass included)"}
-
+        roof["per_step_ms"] = step_breakdown
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base_np = shard.cpu().numpy()
         q_np = q.cpu().numpy()
-        rate, m, t = cpu_sample_rate(w, base_np, q_np, args.cpu_budget)
+        threads = host_threads()
+        rate, m, t = cpu_sample_rate(w, base_np, q_np, args.cpu_budget, threads=threads)
         what = (f"the lists of {m} rows (k + 1 search against all {w['n']} rows, then the "
                 f"row itself dropped)" if is_allnn else
                 f"{m} queries against all {w['n']} base rows")
-        cpu = {"value": rate, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": f"{what} ({t:.1f} s, OpenMP on every host core)"}
+        cpu = {"value": rate, "unit": "queries/s", "cores": threads, "kind": "port",
+               "sample": f"{what} ({t:.1f} s, OpenMP on {threads} host threads)"}
 
     if rank == 0:
         value = w["nq"] * args.steps / (elapsed_ms / 1e3)
@@ -618,17 +700,14 @@ def main():
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("s8" if kname == "hamming_mma" else "u8") if is_hamming else "f16",
             "data": "synthetic (seeded, BASELINE distributions)",
-            "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
-                       "queries": w["nq"], "k": k,
-                       "parallelism": (f"rows to list split over {world} GPU(s), all rows on "
-                                       f"each" if is_allnn else
-                                       f"base rows sharded over {world} GPU(s)"),
-                       "l2_flush": f"{FLUSH_BYTES >> 20} MiB buffer written before every "
-                                   f"timed step (outside the per-step event spans)"},
+            "config": config_of(args, w, world),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(all_launches), "clocks": clocks,
-            "check_vs_oracle_4_queries": check,
+            "parity": parity,
         }
+        if emulated:
+            line["note"] = (f"one GPU searching the shard rank 0 holds at N={args.shard_of} "
+                            f"(rows {lo}..{hi}); a profiling aid, not a bench value")
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -55,6 +55,9 @@ DeviceInfo& device_info() {
   static bool ready[64] = {};
   int dev = 0;
   CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    throw std::runtime_error("[mlxvs_b200] device ordinal " + std::to_string(dev) +
+                             " is beyond the 64 devices this library tracks");
   std::lock_guard<std::mutex> guard(mu);
   DeviceInfo& info = infos[dev];
   if (!ready[dev]) {
@@ -146,6 +149,9 @@ FlagMailbox& flag_mailbox() {
   thread_local FlagMailbox boxes[64];
   int dev = 0;
   CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    throw std::runtime_error("[mlxvs_b200] device ordinal " + std::to_string(dev) +
+                             " is beyond the 64 devices this library tracks");
   FlagMailbox& b = boxes[dev];
   if (b.host == nullptr) {
     CK(cudaHostAlloc(reinterpret_cast<void**>(&b.host), 64, cudaHostAllocDefault));
@@ -1366,13 +1372,19 @@ const NoAllocDevice& noalloc_device() {
   static NoAllocDevice devs[64];
   int dev = 0;
   CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    throw std::runtime_error("[mlxvs_b200] device ordinal " + std::to_string(dev) +
+                             " is beyond the 64 devices this library tracks");
   std::lock_guard<std::mutex> guard(mu);
   NoAllocDevice& d = devs[dev];
   if (d.scratch == nullptr) {
-    int major = 0;
+    int major = 0, minor = 0;
     CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
-    if (major != 10)
-      throw std::runtime_error("[mlxvs_b200] needs an sm_100 GPU (B200)");
+    CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      throw std::runtime_error("[mlxvs_b200] needs an sm_100 GPU (B200); device " +
+                               std::to_string(dev) + " is sm_" + std::to_string(major) +
+                               std::to_string(minor));
     CK(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     void* p = nullptr;
@@ -1407,8 +1419,11 @@ void noalloc_hamming_launch(HammingParams p, const NoAllocDevice& dev, size_t li
   const int fit = (int)std::min<size_t>(64, list_room / per_split);
   p.splits = std::min(choose_splits(p.qblocks, p.tiles, slots, 2.0, 64), fit);
   p.units = p.qblocks * p.splits;
-  kern<<<std::min(p.units, slots), QH + 32, smem, s>>>(p);
-  CK(cudaGetLastError());
+  {
+    ProfScope prof("hamming_topk", s);
+    kern<<<std::min(p.units, slots), QH + 32, smem, s>>>(p);
+    CK(cudaGetLastError());
+  }
   launch_merge(p.partial, p.splits, p.nq_pad, p.nq, p.k, KIND_HAMMING, nullptr, nullptr, ids,
                dist, s);
 }

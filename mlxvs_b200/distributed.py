@@ -15,6 +15,8 @@ merges at :117) with a cross-device one; the reference has no multi-GPU
 path.
 """
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
@@ -45,25 +47,42 @@ def gather_lists(keys, group=None):
     return torch.stack(parts)
 
 
+def _on_stream(stream, device):
+    """Makes `stream` torch's current stream for the block (nothing when it is
+    None).  The search, the NCCL all-gather (which torch queues on its current
+    stream) and every tensor allocated in between then share one stream, so
+    the gather cannot read keys the search has not written yet.  A raw
+    cudaStream_t handle (an int) is wrapped as an external stream."""
+    if stream is None:
+        return contextlib.nullcontext()
+    if isinstance(stream, int):
+        stream = torch.cuda.ExternalStream(stream, device=device)
+    return torch.cuda.stream(stream)
+
+
 def sharded_brute_force_knn(base_shard, queries, k, metric=Metric.l2, *, id_offset, group=None,
                             stream=None):
     """Exact k-NN of queries against the union of every rank's base shard.
 
     base_shard and queries are CUDA tensors (queries identical on every
-    rank); id_offset is the global id of this shard's first row.  Returns
-    (ids int32 [nq, k], distances float32 [nq, k]) on every rank.
+    rank); id_offset is the global id of this shard's first row.  All work,
+    the all-gather included, is queued on `stream` (default: torch's current
+    stream).  Returns (ids int32 [nq, k], distances float32 [nq, k]) on every
+    rank.
     """
     m = _metric(metric)
-    keys = knn_keys(base_shard, queries, k, m, id_offset=id_offset, stream=stream)
-    lists = gather_lists(keys, group)
-    return merge_keys(lists, k, m, queries if m == Metric.l2 else None, stream=stream)
+    with _on_stream(stream, queries.device):
+        keys = knn_keys(base_shard, queries, k, m, id_offset=id_offset)
+        lists = gather_lists(keys, group)
+        return merge_keys(lists, k, m, queries if m == Metric.l2 else None)
 
 
 def sharded_hamming_knn(rows_shard, queries, k, *, id_offset, group=None, stream=None):
     """Hamming version of sharded_brute_force_knn (uint8 codes)."""
-    keys = hamming_keys(rows_shard, queries, k, id_offset=id_offset, stream=stream)
-    lists = gather_lists(keys, group)
-    return merge_keys(lists, k, "hamming", stream=stream)
+    with _on_stream(stream, queries.device):
+        keys = hamming_keys(rows_shard, queries, k, id_offset=id_offset)
+        lists = gather_lists(keys, group)
+        return merge_keys(lists, k, "hamming")
 
 
 def sharded_all_neighbors(rows, k, metric=Metric.l2, *, group=None, stream=None, gather=True):
@@ -72,12 +91,17 @@ def sharded_all_neighbors(rows, k, metric=Metric.l2, *, group=None, stream=None,
     exchange.  Returns (ids, distances) of the whole graph on every rank
     (gather: an all-gather of the lists), else this rank's [hi - lo, k]
     share and its (lo, hi)."""
+    with _on_stream(stream, rows.device):
+        return _sharded_all_neighbors(rows, k, metric, group, gather)
+
+
+def _sharded_all_neighbors(rows, k, metric, group, gather):
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     n = rows.shape[0]
     b = shard_bounds(n, world)
     lo, hi = b[rank], b[rank + 1]
-    ids, dst = all_neighbors_rows(rows, k, metric, begin=lo, end=hi, stream=stream)
+    ids, dst = all_neighbors_rows(rows, k, metric, begin=lo, end=hi)
     if not gather:
         return ids, dst, (lo, hi)
     if world == 1:

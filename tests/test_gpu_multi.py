@@ -1,7 +1,8 @@
 """The row-sharded search on 2 GPUs of one node (NCCL, one process per GPU):
 results equal the single-GPU search (bit for bit on integer data, recall 1
 on float data, where each shard's operand scale may round a score
-differently).  Skipped on a box with fewer than 2 GPUs."""
+differently).  The 2-GPU test is skipped on a box with fewer GPUs; the
+stream= test runs on one."""
 
 import os
 import socket
@@ -70,6 +71,22 @@ def _worker(rank, world, port, out):
                     scores = data.exact_scores(metric, q, b)
                     single = data.recall(ids.cpu().numpy(), scores, k, tol=1e-4) == 1.0
             out[(rank, metric, k, integer)] = (same, single)
+        # stream=: a side stream kept busy first, so a gather queued on
+        # another stream would read keys that are not written yet
+        b, q = make_case("l2", True)
+        bounds = mvd.shard_bounds(b.shape[0], world)
+        lo, hi = bounds[rank], bounds[rank + 1]
+        shard = torch.from_numpy(b[lo:hi]).to(dev)
+        tq = torch.from_numpy(q).to(dev)
+        want = mvd.sharded_brute_force_knn(shard, tq, 10, "l2", id_offset=lo)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            torch.cuda._sleep(200_000_000)
+        got = mvd.sharded_brute_force_knn(shard, tq, 10, "l2", id_offset=lo, stream=side)
+        side.synchronize()
+        out[(rank, "stream")] = bool(torch.equal(got[0], want[0]) and
+                                     torch.equal(got[1], want[1]))
         # the k-NN graph split by rows (all rows on every rank, no exchange
         # but the final gather)
         x, _ = data.gaussian_mixture_int(20_001, 64, 16, seed=44)
@@ -99,3 +116,29 @@ def test_two_gpus_match_single():
                 assert single, (metric, k, integer)
     for r in range(WORLD):
         assert res[(r, "allnn")], r
+        assert res[(r, "stream")], r
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_stream_argument_one_rank():
+    # stream= carries the search and its merge (world size 1 here: no
+    # process group, the gather is the rank's own keys)
+    import mlxvs_b200 as mv
+    from mlxvs_b200 import distributed as mvd
+
+    dev = torch.device("cuda", 0)
+    b, q = make_case("l2", True)
+    tb, tq = torch.from_numpy(b).to(dev), torch.from_numpy(q).to(dev)
+    want = mv.brute_force_knn(tb, tq, 10, "l2")
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        torch.cuda._sleep(100_000_000)
+    ids, dst = mvd.sharded_brute_force_knn(tb, tq, 10, "l2", id_offset=0, stream=side)
+    side.synchronize()
+    assert torch.equal(ids, want[0]) and torch.equal(dst, want[1])
+    # a raw cudaStream_t handle works the same way
+    ids2, dst2 = mvd.sharded_brute_force_knn(tb, tq, 10, "l2", id_offset=0,
+                                             stream=side.cuda_stream)
+    side.synchronize()
+    assert torch.equal(ids2, want[0]) and torch.equal(dst2, want[1])

@@ -64,6 +64,30 @@ def test_matches_allocating_entry_point_on_consecutive_calls():
         assert torch.equal(dist, want_dist)
 
 
+def test_widest_codes_and_a_list_array_that_fills_the_scratch():
+    # 512-byte codes (the widest it reads in place, 128 queries per block),
+    # and nq * k so large that the scratch holds the lists of one base range
+    # only (the array, not the work, sets the number of ranges); two calls
+    # in a row each
+    import torch
+
+    lib, fn = noalloc_entry()
+    cases = [
+        data.hamming_codes(5_000, 512, 256, 0.1, seed=23, nq=300) + (10,),
+        data.hamming_codes(20_000, 16, 2048, 0.1, seed=24, nq=50_000) + (32,),
+    ]
+    for rows_np, q_np, k in cases:
+        rows = torch.from_numpy(rows_np).cuda()
+        q = torch.from_numpy(q_np).cuda()
+        want_ids, want_dist = mv.hamming_knn(rows, q, k)
+        for _ in range(2):
+            rc, ids, dist = run_noalloc(fn, rows, q, k)
+            assert rc == 0, lib.mlxvs_last_error()
+            torch.cuda.synchronize()
+            assert torch.equal(ids, want_ids)
+            assert torch.equal(dist, want_dist)
+
+
 def test_rejects_what_it_cannot_do_without_allocating():
     import torch
 
