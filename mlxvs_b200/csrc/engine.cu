@@ -3,6 +3,7 @@
 // one-pass fp16 path and the split-fp16 path, work decomposition and launches.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -11,6 +12,7 @@
 
 #include "engine.h"
 #include "gemm_topk.cuh"
+#include "gemm_topk_q.cuh"
 #include "hamming.cuh"
 #include "select.cuh"
 #include "knn_kernels.cuh"
@@ -321,11 +323,41 @@ struct GemmMaps {
   CUtensorMap a_hi, a_lo, b_hi, b_lo, b_x;
 };
 
+// The queued epilogue (gemm_topk_q.cuh) is the default wherever it applies;
+// MLXVS_EPILOGUE=inline selects the inline one everywhere (for comparisons).
+bool queued_epilogue_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MLXVS_EPILOGUE");
+    return !(e != nullptr && std::strcmp(e, "inline") == 0);
+  }();
+  return on;
+}
+
+// Ring depth and query-block placement of the queued kernel: at least
+// `min_stages` stages (the inline kernel's depth for the same launch), the
+// resident query block preferred, queues of QK_QD chunks.  Returns false
+// when no such layout fits.
+constexpr int QK_QD = 2;
+bool pick_queued(const DeviceInfo& dev, int npa, int kchunks, int extra, int min_stages,
+                 int* stages, int* a_stream, uint32_t* smem) {
+  const uint32_t budget = (uint32_t)dev.max_smem - 1024u;
+  for (int as : {0, 1}) {
+    for (int st = 8; st >= min_stages; --st) {
+      const QueuedSmem lay = queued_smem(npa, kchunks, st, as, extra, QK_QD);
+      if (lay.total <= budget) {
+        *stages = st;
+        *a_stream = as;
+        *smem = lay.total + 1024u;
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
 template <int QB, int NPASS, int CG, int NBM, int KR, int OP = 0, int MODE = 0>
 void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t smem,
                  cudaStream_t s, const char* prof_name = nullptr) {
-  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP, MODE>;
-  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   ProfScope prof(prof_name ? prof_name
                            : (OP == 1 ? "hamming_mma" : (MODE == 1 ? "gemm_collect" : "gemm_topk")),
                  s);
@@ -335,6 +367,23 @@ void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t s
   const double k_issued = OP == 1 ? 128.0 * p.kchunks
                                   : (double)NPASS * GT_KCH * p.kchunks + 16.0 * p.extra;
   prof.issued = 2.0 * 128.0 * GT_BN * k_issued * (double)p.qblocks * (double)p.tiles;
+  if constexpr (QB == QK_QB && CG == 2 && NPASS == 1 && (KR > 0 || MODE == 1)) {
+    int st = 0, as = 0;
+    uint32_t qsmem = 0;
+    if (queued_epilogue_enabled() &&
+        pick_queued(device_info(), 1, p.kchunks, p.extra, p.stages, &st, &as, &qsmem)) {
+      KnnGemmParams pq = p;
+      pq.stages = st;
+      pq.a_stream = as;
+      auto kern = knn_gemm_topk_queued_kernel<NPASS, NBM, (KR > 0 ? KR : 8), OP, MODE, QK_QD>;
+      CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem));
+      kern<<<grid, QK_THREADS, qsmem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo, m.b_x, pq);
+      CK(cudaGetLastError());
+      return;
+    }
+  }
+  auto kern = knn_gemm_topk_kernel<QB, NPASS, CG, NBM, KR, OP, MODE>;
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   kern<<<grid, GemmLayout<QB, NPASS, CG>::THREADS, smem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo,
                                                               m.b_x, p);
   CK(cudaGetLastError());
