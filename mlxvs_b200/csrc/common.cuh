@@ -108,18 +108,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// A time limit in SM cycles for a limit in nanoseconds: 2 cycles per
+// nanosecond lasts at least as long at any clock up to 2 GHz.  Waits count
+// cycles with clock64 (a register read) rather than reading %globaltimer,
+// which takes on the order of a microsecond: a waiting thread that reads it
+// when its barrier is not yet complete would notice the completion that
+// much later.
+__device__ __forceinline__ long long wait_cycles(uint64_t limit_ns) {
+  return (long long)(2 * limit_ns);
+}
+
 // Waits for the phase of the given parity to complete, for at most about
 // limit_ns (checked every 256 polls).  Returns false when it gave up, or when
 // *abort was raised by another role of the CTA.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t start = globaltimer_ns();
+  const long long start = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - start > limit_ns) return false;
+      if (clock64() - start > wait_cycles(limit_ns)) return false;
     }
   }
 }

@@ -375,7 +375,13 @@ void launch_gemm(const GemmMaps& m, const KnnGemmParams& p, int grid, uint32_t s
       KnnGemmParams pq = p;
       pq.stages = st;
       pq.a_stream = as;
-      auto kern = knn_gemm_topk_queued_kernel<NPASS, NBM, (KR > 0 ? KR : 8), OP, MODE, QK_QD>;
+      // the MMA loop unrolled over the K chunks for the common counts: 2 (fp16
+      // rows of up to 128 values) and 8 (1024-bit codes as int8)
+      constexpr int KQ = KR > 0 ? KR : 8;
+      constexpr int KCH_FIXED = OP == 1 ? 8 : 2;
+      auto kern = p.kchunks == KCH_FIXED
+                      ? knn_gemm_topk_queued_kernel<NPASS, NBM, KQ, OP, MODE, QK_QD, KCH_FIXED>
+                      : knn_gemm_topk_queued_kernel<NPASS, NBM, KQ, OP, MODE, QK_QD, 0>;
       CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem));
       kern<<<grid, QK_THREADS, qsmem, s>>>(m.a_hi, m.a_lo, m.b_hi, m.b_lo, m.b_x, pq);
       CK(cudaGetLastError());

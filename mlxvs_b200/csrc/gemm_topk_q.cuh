@@ -20,10 +20,16 @@
 //                       queues, and the warp inserts the chunks' candidates
 //                       (one per lane per step, all lanes at once); the
 //                       list's worst key is the query's floor, published to
-//                       the filter warps through shared memory and to the
-//                       other units of the query through a global atomicMax.
+//                       the filter warps and the relay warp through shared
+//                       memory.
 //   warp 12             TMA producer (as in the inline kernel).
 //   warp 13             TMEM allocation and MMA issue (as in the inline kernel).
+//   warp 14             floor relay: publishes each query's list floor to the
+//                       global shared floor (atomicMax) and brings the other
+//                       units' floors back into shared memory, so that the
+//                       filter and select loops never touch global memory
+//                       between a unit's start and its end (a CTA-scope fence
+//                       there would wait for the outstanding global access).
 //
 // Why: with one query per lane a 32-lane warp takes a slow path whenever any
 // of its 32 queries has a candidate, and at k = 10 on 10^5-10^6 rows that is
@@ -52,7 +58,8 @@ constexpr int QK_FILTER_WARPS = 8;
 constexpr int QK_SELECT_WARPS = 4;
 constexpr int QK_PRODUCER = QK_FILTER_WARPS + QK_SELECT_WARPS;  // warp 12
 constexpr int QK_MMA = QK_PRODUCER + 1;                          // warp 13
-constexpr int QK_THREADS = (QK_MMA + 1) * 32;                    // 448
+constexpr int QK_FLOORS = QK_MMA + 1;                            // warp 14
+constexpr int QK_THREADS = (QK_FLOORS + 1) * 32;                 // 480
 constexpr int QK_QB = 128;                                       // queries per unit
 // Select warps finish a unit at most 1 + QD units apart (a filter warp is
 // at most QD end markers ahead of its select warp, and the filter warps are
@@ -73,8 +80,9 @@ struct QueuedSmem {
   uint32_t q_off;           // queues: scores [2][QD][4][128] float4, cols [2][QD][128]
   uint32_t qcol_off;
   uint32_t qtail_off, qhead_off;  // [2][128] u32 each
-  uint32_t thr_off;               // [128] u64: (unit tag << 32) | threshold bits
-  uint32_t misc_off;              // unit-end counters, a ring of QK_END_RING
+  uint32_t thr_off;               // [128] u64: (unit tag << 32) | threshold bits, the list's
+  uint32_t gthr_off;              // [128] u64: the same for the other units' floors
+  uint32_t misc_off;              // unit-end counters (a ring of QK_END_RING), units finished
   uint32_t bar_off;
   uint32_t total;
 };
@@ -94,14 +102,23 @@ __host__ __device__ inline QueuedSmem queued_smem(int npa, int kchunks, int stag
   s.qtail_off = s.qcol_off + (uint32_t)(2 * qd * QK_QB * 4);
   s.qhead_off = s.qtail_off + 2u * QK_QB * 4u;
   s.thr_off = s.qhead_off + 2u * QK_QB * 4u;
-  s.misc_off = s.thr_off + (uint32_t)QK_QB * 8u;
-  s.bar_off = s.misc_off + 4u * QK_END_RING;
+  s.gthr_off = s.thr_off + (uint32_t)QK_QB * 8u;
+  s.misc_off = s.gthr_off + (uint32_t)QK_QB * 8u;
+  s.bar_off = s.misc_off + 4u * QK_END_RING + 16u;
   // full[stages], empty[stages], a_full, a_empty, acc_full[2], acc_empty[2], aux
   s.total = s.bar_off + (uint32_t)(2 * stages + 7) * 8u + 16u;
   return s;
 }
 
 #ifdef __CUDACC__
+
+// Time limits inside the hot loops count SM cycles (clock64, a register
+// read) instead of reading %globaltimer, which takes about a microsecond and
+// would stall a select warp that polls its queues.  At most 2 GHz, a limit of
+// 2 cycles per nanosecond lasts at least as long as the nanosecond limit.
+__device__ __forceinline__ long long qk_cycle_limit(uint64_t limit_ns) {
+  return (long long)(2 * limit_ns);
+}
 
 // Copies one 16-score chunk into this lane's queue of its column half.
 // Returns false when the wait for a free slot gave up (abort raised, or the
@@ -111,11 +128,11 @@ __device__ __forceinline__ bool qk_push(const float* v, int32_t col, float4* qs,
                                         volatile uint32_t* tail_p, volatile uint32_t* head_p,
                                         uint32_t& tail, volatile int* abort, uint64_t limit_ns) {
   if (tail - *head_p >= (uint32_t)QD) {
-    const uint64_t start = globaltimer_ns();
+    const long long start = clock64();
     for (uint32_t i = 1; tail - *head_p >= (uint32_t)QD; ++i) {
       if ((i & 63u) == 0) {
         if (*abort) return false;
-        if (globaltimer_ns() - start > limit_ns) return false;
+        if (clock64() - start > qk_cycle_limit(limit_ns)) return false;
       }
     }
   }
@@ -212,7 +229,46 @@ __device__ __forceinline__ void qk_filter32(const uint32_t (&r)[32], const float
   }
 }
 
-template <int NPASS, int NBM, int KR, int OP, int MODE, int QD>
+// The MMAs of one tile when its number of K chunks is known at compile time:
+// for each chunk, wait for its stage, issue its four MMAs back to back and
+// release the stage.  The tensor core's instruction queue is shallow: a few
+// dozen instructions between two MMAs (descriptor arithmetic, a loop branch,
+// a modulo) leave it idle, so descriptors advance by constants (start
+// addresses in 16-byte units), the chunk loop is unrolled and the ring
+// position wraps without a branch.  Returns false when a wait gave up.
+template <int KCH, int OP>
+__device__ __forceinline__ bool qk_mma_tile(uint32_t d_tmem, uint64_t da0, bool a_stream,
+                                            uint64_t db0, uint32_t stage_units,
+                                            uint32_t a_in_stage_units, bool extra, uint64_t dax,
+                                            uint64_t dbx, uint32_t& stage, uint32_t& phase,
+                                            uint32_t stages, uint64_t* full, uint64_t* empty,
+                                            volatile int* abort, uint64_t wait_ns,
+                                            uint32_t idesc) {
+#pragma unroll
+  for (int kc = 0; kc < KCH; ++kc) {
+    if (!mbar_wait(&full[stage], phase, abort, wait_ns)) return false;
+    tc_fence_after();
+    const uint64_t db = db0 + (uint64_t)(stage * stage_units);
+    const uint64_t da =
+        a_stream ? db + a_in_stage_units : da0 + (uint64_t)(kc * (GT_ACHUNK >> 4));
+    if (kc == 0 && extra) umma_f16_ss(d_tmem, dax, dbx, idesc, 0u);
+#pragma unroll
+    for (int kk = 0; kk < GT_KCH / 16; ++kk) {
+      const uint32_t acc_in = (kc | kk) != 0 || extra;
+      if constexpr (OP == 1)
+        umma_i8_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, acc_in);
+      else
+        umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, acc_in);
+    }
+    umma_commit(&empty[stage]);
+    const uint32_t next = stage + 1;
+    phase ^= next == stages ? 1u : 0u;
+    stage = next == stages ? 0u : next;
+  }
+  return true;
+}
+
+template <int NPASS, int NBM, int KR, int OP, int MODE, int QD, int KCH = 0>
 __global__ void __launch_bounds__(QK_THREADS, 1)
     knn_gemm_topk_queued_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                                 const __grid_constant__ CUtensorMap tm_a_lo,
@@ -241,7 +297,10 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
   volatile uint32_t* qhead = reinterpret_cast<volatile uint32_t*>(smem + lay.qhead_off);
   volatile unsigned long long* sthr =
       reinterpret_cast<volatile unsigned long long*>(smem + lay.thr_off);
+  volatile unsigned long long* gthr =
+      reinterpret_cast<volatile unsigned long long*>(smem + lay.gthr_off);
   uint32_t* unit_end = reinterpret_cast<uint32_t*>(smem + lay.misc_off);
+  volatile uint32_t* units_done = unit_end + QK_END_RING;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + lay.bar_off);
   uint64_t* full = bars;
   uint64_t* empty = bars + p.stages;
@@ -272,13 +331,17 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
     }
     *abort_flag = 0;
     for (int i = 0; i < QK_END_RING; ++i) unit_end[i] = 0u;
+    *units_done = 0u;
     fence_barrier_init();
   }
   for (int i = threadIdx.x; i < 2 * QB; i += blockDim.x) {
     qtail[i] = 0u;
     qhead[i] = 0u;
   }
-  for (int i = threadIdx.x; i < QB; i += blockDim.x) sthr[i] = 0ull;
+  for (int i = threadIdx.x; i < QB; i += blockDim.x) {
+    sthr[i] = 0ull;
+    gthr[i] = 0ull;
+  }
   if (warp == QK_MMA) {
     tmem_alloc(tmem_slot, 2 * GT_BN);
     tmem_relinquish();
@@ -397,6 +460,32 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
           }
           tc_fence_after();
         }
+        if constexpr (KCH > 0) {
+          // the lean form (the chunk count of this instantiation)
+          const uint64_t da0 = sdesc_k128(smem_u32(a_res));
+          const uint64_t db0 = sdesc_k128(smem_u32(stage_base));
+          const uint64_t dax = sdesc_k32(smem_u32(ax));
+          const uint64_t dbx0 = sdesc_k32(smem_u32(x_ring));
+          uint32_t xs = lay.x_slots ? tcount % lay.x_slots : 0u;
+          for (int t = t0; t < t1 && ok; ++t, ++tcount) {
+            if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, abort_flag, p.wait_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            ok = qk_mma_tile<KCH, OP>(
+                tmem_base + acc * GT_BN, da0, p.a_stream != 0, db0, lay.stage_bytes >> 4,
+                (uint32_t)(NPA * GT_BCHUNK) >> 4, p.extra != 0, dax,
+                dbx0 + (uint64_t)(xs * (GT_XCHUNK >> 4)), stage, phase, (uint32_t)p.stages, full,
+                empty, abort_flag, p.wait_ns, IDESC);
+            if (!ok) break;
+            umma_commit(&acc_full[acc]);
+            acc ^= 1;
+            acc_ph ^= acc == 0 ? 1u : 0u;
+            const uint32_t xn = xs + 1;
+            xs = xn == lay.x_slots ? 0u : xn;
+          }
+        } else
         for (int t = t0; t < t1 && ok; ++t, ++tcount) {
           if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, abort_flag, p.wait_ns)) {
             ok = false;
@@ -484,19 +573,18 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
       const uint64_t tag = (uint64_t)(uidx + 1) << 32;
       const unsigned long long* gfl_q = p.gfloor + split * p.gfloor_split_stride + q;
       // padding rows offer nothing; the others start from the shared floor
+      // (read once here; later rises arrive through shared memory)
       float thr = q_ok ? key_score(*reinterpret_cast<const volatile unsigned long long*>(gfl_q))
                        : INFINITY;
-      unsigned long long gnext = q_ok ? *reinterpret_cast<const volatile unsigned long long*>(gfl_q)
-                                      : 0ull;
       for (int t = t0; t < t1 && ok; ++t) {
         if (MODE == 0 && q_ok) {
-          // the select warp's floor of this unit (a tile old at most) and
-          // the shared floor loaded one tile ago
-          const unsigned long long x = sthr[row];
+          // the select warp's floor of this unit and the other units' floor
+          // as relayed (each a tile old at most)
+          const unsigned long long x = sthr[row], g = gthr[row];
           if ((x & 0xFFFFFFFF00000000ull) == tag)
             thr = fmaxf(thr, __uint_as_float((uint32_t)x));
-          thr = fmaxf(thr, key_score(gnext));
-          gnext = *reinterpret_cast<const volatile unsigned long long*>(gfl_q);
+          if ((g & 0xFFFFFFFF00000000ull) == tag)
+            thr = fmaxf(thr, __uint_as_float((uint32_t)g));
         }
         // one answer for the whole warp: the TMEM loads below are collective
         if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_ph, abort_flag, p.wait_ns))) {
@@ -580,8 +668,10 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
         }
         floor = key[0];
       }
-      uint64_t gpub = q_ok ? *reinterpret_cast<volatile unsigned long long*>(gfl_q) : 0ull;
-      if (gpub > floor) floor = gpub;
+      {
+        const uint64_t g = q_ok ? *reinterpret_cast<volatile unsigned long long*>(gfl_q) : 0ull;
+        if (g > floor) floor = g;
+      }
       float thr = key_score(floor);
       if (MODE == 0) sthr[row] = tag | __float_as_uint(thr);
       // collect mode: this unit's buffers and counts per column half
@@ -594,7 +684,7 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
       }
       uint32_t ended = 0;  // bit c: the end marker of column half c was seen
       uint32_t pref = 0;
-      uint64_t idle_since = 0;
+      long long idle_since = 0;
       for (;;) {
         // each lane takes at most one chunk of its query's queues
         uint32_t mask = 0, id0 = 0, ent = 0, ech = 0;
@@ -666,36 +756,33 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
             }
           }
         }
-        if (MODE == 0 && floor != floor_before) {
-          sthr[row] = tag | __float_as_uint(thr);
-          if (q_ok && floor > gpub) {
-            atomicMax(gfl_q, (unsigned long long)floor);
-            gpub = floor;
-          }
-        }
+        if (MODE == 0 && floor != floor_before) sthr[row] = tag | __float_as_uint(thr);
         if (__all_sync(0xffffffffu, ended == 3u)) break;
         if (!__any_sync(0xffffffffu, got)) {
-          // nothing queued: pick up other units' floors, then wait a little
+          // nothing queued: pick up the other units' floor as relayed (its
+          // score with the lowest id part: at or below their true floor)
           if (MODE == 0 && q_ok) {
-            const unsigned long long g = *reinterpret_cast<volatile unsigned long long*>(gfl_q);
-            if (g > floor) {
-              floor = g;
-              gpub = g;
-              thr = key_score(floor);
-              sthr[row] = tag | __float_as_uint(thr);
+            const unsigned long long g = gthr[row];
+            if ((g & 0xFFFFFFFF00000000ull) == tag) {
+              const uint64_t gk = (uint64_t)order_bits(__uint_as_float((uint32_t)g)) << 32;
+              if (gk > floor) {
+                floor = gk;
+                thr = key_score(floor);
+                sthr[row] = tag | __float_as_uint(thr);
+              }
             }
           }
-          const uint64_t now = globaltimer_ns();
+          const long long now = clock64();
           if (idle_since == 0) {
             idle_since = now;
-          } else if (now - idle_since > p.wait_ns || *abort_flag) {
+          } else if (now - idle_since > qk_cycle_limit(p.wait_ns) || *abort_flag) {
             ok = false;
           }
           if (__any_sync(0xffffffffu, !ok)) {
             ok = false;
             break;
           }
-          __nanosleep(64);
+          __nanosleep(32);
         } else {
           idle_since = 0;
         }
@@ -720,6 +807,7 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
             *cnt = 0u;
             __threadfence();
             atomicMax(p.done + qb, split + 1);
+            atomicMax(const_cast<uint32_t*>(units_done), uidx + 1);
           }
         }
       }
@@ -727,6 +815,57 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
     if (!ok) {
       *abort_flag = 1;
       atomicOr(p.err, ERR_WAIT_EPILOGUE);
+    }
+  } else if (warp == QK_FLOORS && MODE == 0) {
+    // ------------------------------------------------------------ relay
+    // lane l serves rows l, l + 32, l + 64, l + 96 of the block: each round
+    // publishes the list floors that rose (their scores, with the lowest id
+    // part) and brings back the shared floor where it beats the list's
+    uint32_t uidx = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uidx) {
+      const int qb = u % p.qblocks;
+      const int split = u / p.qblocks;
+      const uint64_t tag = (uint64_t)(uidx + 1) << 32;
+      unsigned long long* gfl[4];
+      bool qk[4];
+      uint64_t known[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int64_t q = (int64_t)qb * QB + lane + 32 * r;
+        qk[r] = q < p.nq;
+        gfl[r] = p.gfloor + split * p.gfloor_split_stride + q;
+        known[r] = 0ull;
+      }
+      const long long start = clock64();
+      while (*units_done <= uidx) {
+        unsigned long long g[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          g[r] = qk[r] ? *reinterpret_cast<volatile unsigned long long*>(gfl[r]) : 0ull;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (!qk[r]) continue;
+          const int row = lane + 32 * r;
+          const unsigned long long x = sthr[row];
+          if ((x & 0xFFFFFFFF00000000ull) == tag) {
+            const uint64_t mine = (uint64_t)order_bits(__uint_as_float((uint32_t)x)) << 32;
+            if (mine > known[r] && mine > g[r]) {
+              atomicMax(gfl[r], (unsigned long long)mine);
+              known[r] = mine;
+            }
+          }
+          if (g[r] > known[r]) {
+            known[r] = g[r];
+            gthr[row] = tag | __float_as_uint(key_score(g[r]));
+          }
+        }
+        if (*abort_flag || clock64() - start > qk_cycle_limit(p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        __nanosleep(200);
+      }
     }
   }
 
