@@ -1,7 +1,8 @@
 """Builds libmlxvs_b200.so in-tree with nvcc for sm_100a.
 
 Usage: python -m mlxvs_b200.build [--verbose]
-The library exports only the C API of include/mlxvs_c.h (the rest is hidden).
+The library exports the C API of include/mlxvs_c.h and the C++ API of
+include/mlxvs.h (the rest is hidden).
 """
 
 import os
@@ -13,9 +14,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmlxvs_b200.so")
-SOURCES = ["engine.cu", "c_api.cpp"]
-HEADERS = ["common.cuh", "gemm_topk.cuh", "hamming.cuh", "knn_kernels.cuh", "select.cuh",
-           "engine.h"]
+SOURCES = ["engine.cu", "c_api.cpp", "cpp_api.cu"]
+HEADERS = ["common.cuh", "gemm_topk.cuh", "gemm_topk_q.cuh", "hamming.cuh", "knn_kernels.cuh",
+           "select.cuh", "engine.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -48,7 +49,7 @@ def stale():
         return True
     t = os.path.getmtime(LIB)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
-    deps.append(os.path.join(ROOT, "include", "mlxvs_c.h"))
+    deps += [os.path.join(ROOT, "include", h) for h in ("mlxvs_c.h", "mlxvs.h")]
     return any(os.path.getmtime(p) > t for p in deps)
 
 

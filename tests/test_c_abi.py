@@ -44,6 +44,8 @@ def test_exports_nothing_else():
     out = subprocess.run(["nm", "-D", "--defined-only", mv.library_path()],
                          capture_output=True, text=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    # the C++ API of include/mlxvs.h (namespace mlxvs) is checked in test_cpp_api
+    exported = {s for s in exported if not s.startswith("_ZN5mlxvs")}
     assert exported == set(declared_functions())
 
 
