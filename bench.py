@@ -279,6 +279,8 @@ def config_of(args, w, world):
                        f"(outside the per-step event spans)"}
     if getattr(args, "shard_of", 1) > 1:
         cfg["shard_of"] = args.shard_of
+    if getattr(args, "entry", "default") == "noalloc":
+        cfg["entry"] = "mlxvs_hamming_knn_noalloc (popcount kernel)"
     return cfg
 
 
@@ -428,6 +430,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the post-timing comparison with the oracle")
+    ap.add_argument("--entry", default="default", choices=["default", "noalloc"],
+                    help="Hamming workloads at N=1: noalloc times mlxvs_hamming_knn_noalloc "
+                         "(the popcount kernel, caller-owned outputs) instead of "
+                         "mlxvs_hamming_knn_device")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="one process searching the shard rank 0 holds at N GPUs (for "
                          "per-rank profiles on one GPU); the line is not a bench value")
@@ -477,6 +483,12 @@ def main():
     is_hamming = w["kind"] == "hamming"
     metric = None if is_hamming else w["metric"]
     stream = torch.cuda.current_stream(dev)
+    noalloc_out = None
+    if args.entry == "noalloc":
+        if not is_hamming or world > 1:
+            raise SystemExit("--entry noalloc is for Hamming workloads at N=1")
+        noalloc_out = (torch.empty((w["nq"], k), dtype=torch.int32, device=dev),
+                       torch.empty((w["nq"], k), dtype=torch.float32, device=dev))
 
     def step():
         if is_allnn:
@@ -484,6 +496,8 @@ def main():
                 return mv.all_neighbors(shard, k, metric, algo="brute_force")
             return mv.all_neighbors_rows(shard, k, metric, begin=lo, end=hi)
         if world == 1:
+            if is_hamming and noalloc_out is not None:
+                return mv.hamming_knn_noalloc(shard, q, k, *noalloc_out)
             if is_hamming:
                 return mv.hamming_knn(shard, q, k)
             return mv.brute_force_knn(shard, q, k, metric)
@@ -557,6 +571,34 @@ def main():
     all_launches = all_launches * args.steps // max(prof_steps, 1)
     mv.profile_enable(False)
     mv.synchronize()
+    if world > 1 and not is_allnn:
+        # the sharded step in its three parts, each bracketed by CUDA events
+        # on the launching stream: this rank's search (prep, fused kernel,
+        # merge of its units' lists), the NCCL all-gather of the [nq, k]
+        # keys (which also waits for the slowest rank), the final merge
+        parts = {"rank_search": 0.0, "all_gather": 0.0, "final_merge": 0.0}
+        kind = "hamming" if is_hamming else metric
+        mq = q if metric == "l2" else None
+        for i in range(prof_steps):
+            flush.fill_(i & 0x7F)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record(stream)
+            keys = (mv.hamming_keys(shard, q, k, id_offset=lo) if is_hamming else
+                    mv.knn_keys(shard, q, k, metric, id_offset=lo))
+            ev[1].record(stream)
+            lists = mvd.gather_lists(keys)
+            ev[2].record(stream)
+            mv.merge_keys(lists, k, kind, mq)
+            ev[3].record(stream)
+            torch.cuda.synchronize()
+            for name, a, b in (("rank_search", 0, 1), ("all_gather", 1, 2),
+                               ("final_merge", 2, 3)):
+                parts[name] += ev[a].elapsed_time(ev[b]) / prof_steps
+        step_breakdown.update(parts)
+        # the slowest rank's fused kernel sets when the all-gather can finish
+        t = torch.tensor([kern_ms / max(kern_launches, 1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_breakdown["kernel_max_over_ranks"] = float(t.item())
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -626,7 +668,9 @@ def main():
     if kern_launches > 0:
         per_launch_s = kern_ms / kern_launches / 1e3
         n_local = hi - lo
-        traffic, traffic_src = load_traffic(args.workload, args.shard_of if emulated else world)
+        traffic, traffic_src = load_traffic(
+            args.workload + ("+noalloc" if noalloc_out is not None else ""),
+            args.shard_of if emulated else world)
         if is_hamming and kname == "hamming_mma":
             # codes as +-1 int8 on the tensor cores: 2 * Q * N * bits integer
             # ops per launch, against twice the measured bf16 rate (int8 runs

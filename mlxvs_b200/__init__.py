@@ -34,6 +34,7 @@ __all__ = [
     "topk_merge",
     "refine",
     "hamming_knn",
+    "hamming_knn_noalloc",
     "knn_keys",
     "hamming_keys",
     "merge_keys",
@@ -75,6 +76,7 @@ def _load():
         "mlxvs_hamming_knn": [p, i64, p, i64, i32, i32, p, p],
         "mlxvs_brute_force_knn_device": [p, i64, p, i64, i32, i32, ctypes.c_int, p, p, p],
         "mlxvs_hamming_knn_device": [p, i64, p, i64, i32, i32, p, p, p],
+        "mlxvs_hamming_knn_noalloc": [p, i64, p, i64, i32, i32, p, p, p],
         "mlxvs_knn_keys_device": [p, i64, p, i64, i32, i32, ctypes.c_int, i64, p, p],
         "mlxvs_hamming_keys_device": [p, i64, p, i64, i32, i32, i64, p, p],
         "mlxvs_all_neighbors": [p, i64, i32, i32, ctypes.c_int, p, p],
@@ -462,6 +464,32 @@ def hamming_knn(rows, queries, k, *, stream=None):
     _check(lib.mlxvs_hamming_knn(
         r.ctypes.data, r.shape[0], q.ctypes.data, nq, r.shape[1], k,
         ids.ctypes.data, dist.ctypes.data))
+    return ids, dist
+
+
+def hamming_knn_noalloc(rows, queries, k, ids, dist, *, stream=None):
+    """hamming_knn into caller-owned outputs, with no device allocation
+    (mlxvs_hamming_knn_noalloc): rows and queries are uint8 CUDA tensors,
+    ids int32 and dist float32 CUDA tensors of shape [nq, k].  Its scratch is
+    one static array per GPU, so calls must not overlap and
+    nq * (k + 1) * 8 bytes must fit in 16 MiB."""
+    op = "mlxvs::hamming_knn"
+    lib = _load()
+    torch = _torch()
+    for t, nm in ((rows, "rows"), (queries, "queries")):
+        if not (_is_torch(t) and t.is_cuda and t.dim() == 2 and t.dtype == torch.uint8
+                and t.is_contiguous()):
+            raise ValueError(f"[{op}] {nm} must be bit-packed uint8 [n, bytes] on a CUDA "
+                             "device, contiguous.")
+    nq, k = queries.shape[0], int(k)
+    for t, dt, nm in ((ids, torch.int32, "ids"), (dist, torch.float32, "dist")):
+        if not (_is_torch(t) and t.is_cuda and t.dtype == dt and tuple(t.shape) == (nq, k)
+                and t.is_contiguous()):
+            raise ValueError(f"[{op}] {nm} must be a contiguous CUDA tensor [nq, k] of {dt}.")
+    with torch.cuda.device(queries.device):
+        _check(lib.mlxvs_hamming_knn_noalloc(
+            rows.data_ptr(), rows.shape[0], queries.data_ptr(), nq, rows.shape[1], k,
+            ids.data_ptr(), dist.data_ptr(), _stream_handle(stream, queries.device)))
     return ids, dist
 
 
