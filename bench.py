@@ -279,6 +279,10 @@ def config_of(args, w, world):
                        f"(outside the per-step event spans)"}
     if getattr(args, "shard_of", 1) > 1:
         cfg["shard_of"] = args.shard_of
+    if world > 1 and not is_allnn:
+        cfg["exchange"] = ("peer memory over NVLink (PeerExchange)"
+                           if getattr(args, "exchange", "peer") == "peer" and w["k"] <= 32
+                           and world * w["k"] <= 768 and world <= 8 else "NCCL all-gather")
     if getattr(args, "entry", "default") == "noalloc":
         cfg["entry"] = "mlxvs_hamming_knn_noalloc (popcount kernel)"
     return cfg
@@ -434,6 +438,9 @@ def main():
                     help="Hamming workloads at N=1: noalloc times mlxvs_hamming_knn_noalloc "
                          "(the popcount kernel, caller-owned outputs) instead of "
                          "mlxvs_hamming_knn_device")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: the ranks' key lists merged from peer memory over NVLink "
+                         "(PeerExchange) or through an NCCL all-gather")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="one process searching the shard rank 0 holds at N GPUs (for "
                          "per-rank profiles on one GPU); the line is not a bench value")
@@ -490,6 +497,12 @@ def main():
         noalloc_out = (torch.empty((w["nq"], k), dtype=torch.int32, device=dev),
                        torch.empty((w["nq"], k), dtype=torch.float32, device=dev))
 
+    # N > 1: one exchange buffer per rank for every step's key lists
+    exch = None
+    if world > 1 and not is_allnn and args.exchange == "peer" and \
+            world <= mvd.PeerExchange.MAX_WORLD and k <= 32 and world * k <= 768:
+        exch = mvd.PeerExchange(w["nq"] * k)
+
     def step():
         if is_allnn:
             if world == 1 and not emulated:
@@ -502,8 +515,8 @@ def main():
                 return mv.hamming_knn(shard, q, k)
             return mv.brute_force_knn(shard, q, k, metric)
         if is_hamming:
-            return mvd.sharded_hamming_knn(shard, q, k, id_offset=lo)
-        return mvd.sharded_brute_force_knn(shard, q, k, metric, id_offset=lo)
+            return mvd.sharded_hamming_knn(shard, q, k, id_offset=lo, exchange=exch)
+        return mvd.sharded_brute_force_knn(shard, q, k, metric, id_offset=lo, exchange=exch)
 
     for _ in range(args.warmup):
         step()
@@ -572,28 +585,41 @@ def main():
     mv.profile_enable(False)
     mv.synchronize()
     if world > 1 and not is_allnn:
-        # the sharded step in its three parts, each bracketed by CUDA events
-        # on the launching stream: this rank's search (prep, fused kernel,
-        # merge of its units' lists), the NCCL all-gather of the [nq, k]
-        # keys (which also waits for the slowest rank), the final merge
-        parts = {"rank_search": 0.0, "all_gather": 0.0, "final_merge": 0.0}
+        # the sharded step in its parts, each bracketed by CUDA events on the
+        # launching stream: this rank's search (prep, fused kernel, merge of
+        # its units' lists), then either the peer exchange's merge (its wait
+        # for every rank's keys included) or the NCCL all-gather of the
+        # [nq, k] keys (which also waits for the slowest rank) and the merge
         kind = "hamming" if is_hamming else metric
         mq = q if metric == "l2" else None
+        names = (("rank_search", "exchange_merge") if exch is not None else
+                 ("rank_search", "all_gather", "final_merge"))
+        parts = {n: 0.0 for n in names}
         for i in range(prof_steps):
             flush.fill_(i & 0x7F)
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
             ev[0].record(stream)
-            keys = (mv.hamming_keys(shard, q, k, id_offset=lo) if is_hamming else
-                    mv.knn_keys(shard, q, k, metric, id_offset=lo))
-            ev[1].record(stream)
-            lists = mvd.gather_lists(keys)
-            ev[2].record(stream)
-            mv.merge_keys(lists, k, kind, mq)
-            ev[3].record(stream)
+            if exch is not None:
+                if is_hamming:
+                    exch.hamming_keys(shard, q, k, lo)
+                    ev[1].record(stream)
+                    exch.merge(q.shape[0], k, "hamming")
+                else:
+                    qf = exch.knn_keys(shard, q, k, metric, lo)
+                    ev[1].record(stream)
+                    exch.merge(q.shape[0], k, metric, qf)
+                ev[2].record(stream)
+            else:
+                keys = (mv.hamming_keys(shard, q, k, id_offset=lo) if is_hamming else
+                        mv.knn_keys(shard, q, k, metric, id_offset=lo))
+                ev[1].record(stream)
+                lists = mvd.gather_lists(keys)
+                ev[2].record(stream)
+                mv.merge_keys(lists, k, kind, mq)
+                ev[3].record(stream)
             torch.cuda.synchronize()
-            for name, a, b in (("rank_search", 0, 1), ("all_gather", 1, 2),
-                               ("final_merge", 2, 3)):
-                parts[name] += ev[a].elapsed_time(ev[b]) / prof_steps
+            for j, name in enumerate(names):
+                parts[name] += ev[j].elapsed_time(ev[j + 1]) / prof_steps
         step_breakdown.update(parts)
         # the slowest rank's fused kernel sets when the all-gather can finish
         t = torch.tensor([kern_ms / max(kern_launches, 1)], dtype=torch.float64, device=dev)
@@ -632,9 +658,10 @@ def main():
                     return i.cpu(), d_.cpu()
                 qd = q_h.to(dev, non_blocking=True)
                 if is_hamming:
-                    i, d_ = mvd.sharded_hamming_knn(sd, qd, k, id_offset=lo)
+                    i, d_ = mvd.sharded_hamming_knn(sd, qd, k, id_offset=lo, exchange=exch)
                 else:
-                    i, d_ = mvd.sharded_brute_force_knn(sd, qd, k, metric, id_offset=lo)
+                    i, d_ = mvd.sharded_brute_force_knn(sd, qd, k, metric, id_offset=lo,
+                                                        exchange=exch)
                 return i.cpu(), d_.cpu()
         e2e_step()
         torch.cuda.synchronize()
@@ -753,6 +780,10 @@ def main():
             line["note"] = (f"one GPU searching the shard rank 0 holds at N={args.shard_of} "
                             f"(rows {lo}..{hi}); a profiling aid, not a bench value")
         print(json.dumps(line), flush=True)
+    if exch is not None:
+        torch.cuda.synchronize()
+        barrier()
+        exch.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

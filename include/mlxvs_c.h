@@ -310,6 +310,41 @@ MLXVS_C_API int mlxvs_merge_keys_device(
     void* stream);
 
 /**
+ * Exchange of the row shards' key lists between the GPUs of one node (one
+ * process per GPU), replacing an all-gather of the lists followed by
+ * mlxvs_merge_keys_device: each GPU writes its [nq, k] keys of a step
+ * (mlxvs_knn_keys_device / mlxvs_hamming_keys_device) into its slot of the
+ * step's epoch (mlxvs_exchange_keys), then mlxvs_exchange_merge_device
+ * publishes them, waits until every GPU has published the same epoch
+ * (bounded; a wait that gives up makes that step's results missing and is
+ * reported by mlxvs_device_synchronize) and merges the world's lists,
+ * reading the peers' slots over NVLink.  Epochs start at 1 and rise by one
+ * per step, the same on every GPU.  Set-up: mlxvs_exchange_create on every
+ * GPU (world <= 8, capacity >= nq * k keys), exchange the 64-byte handles
+ * (mlxvs_exchange_handle) between the processes, mlxvs_exchange_open each
+ * peer's.  The merge needs k <= 32 and world * k <= 768.
+ * Replaces: the cross-tile merge of src/knn.cpp:117 across devices (no
+ * counterpart in the reference, which runs on one device).
+ */
+MLXVS_C_API int mlxvs_exchange_create(int32_t world, int32_t rank, int64_t capacity_keys,
+                                      void** exchange);
+MLXVS_C_API int mlxvs_exchange_handle(void* exchange, uint8_t* handle);
+MLXVS_C_API int mlxvs_exchange_open(void* exchange, int32_t peer, const uint8_t* handle);
+MLXVS_C_API int mlxvs_exchange_keys(void* exchange, uint32_t epoch, uint64_t** keys);
+MLXVS_C_API int mlxvs_exchange_merge_device(
+    void* exchange,
+    uint32_t epoch,
+    int64_t nq,
+    int32_t k,
+    int32_t kind,
+    const float* queries,
+    int32_t d,
+    int32_t* ids,
+    float* distances,
+    void* stream);
+MLXVS_C_API int mlxvs_exchange_destroy(void* exchange);
+
+/**
  * Waits for stream and reports any error the library's kernels recorded on
  * the current device since the last call (a bounded wait that gave up).
  * Not in the reference (MLX reports errors at mx::eval).

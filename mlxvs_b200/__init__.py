@@ -86,6 +86,12 @@ def _load():
         "mlxvs_refine_device": [p, i64, i32, p, i64, p, i32, i32, ctypes.c_int, p, p, p],
         "mlxvs_all_neighbors_device": [p, i64, i32, i32, ctypes.c_int, i64, i64, p, p, p],
         "mlxvs_merge_keys_device": [p, i32, i64, i32, i32, p, i32, p, p, p],
+        "mlxvs_exchange_create": [i32, i32, i64, ctypes.POINTER(ctypes.c_void_p)],
+        "mlxvs_exchange_handle": [p, p],
+        "mlxvs_exchange_open": [p, i32, p],
+        "mlxvs_exchange_keys": [p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p)],
+        "mlxvs_exchange_merge_device": [p, ctypes.c_uint32, i64, i32, i32, p, i32, p, p, p],
+        "mlxvs_exchange_destroy": [p],
         "mlxvs_device_synchronize": [p],
         "mlxvs_profile_enable": [i32],
         "mlxvs_profile_read": [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),

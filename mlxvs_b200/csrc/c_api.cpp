@@ -391,7 +391,7 @@ int mlxvs_brute_force_knn_device(const float* base, int64_t n, const float* quer
                                  int32_t d, int32_t k, mlxvs_metric metric, int32_t* ids,
                                  float* distances, void* stream) {
   return guarded([&] {
-    require(ids != nullptr, "ids must not be NULL.");
+    require(ids != nullptr || nq == 0, "ids must not be NULL.");
     host_rows(base, n, d);
     host_rows(queries, nq, d);
     mlxvs_b200::brute_force_knn(base, n, queries, nq, d, k, to_metric(metric), ids, distances,
@@ -403,7 +403,7 @@ int mlxvs_hamming_knn_device(const uint8_t* rows, int64_t n, const uint8_t* quer
                              int32_t bytes, int32_t k, int32_t* ids, float* distances,
                              void* stream) {
   return guarded([&] {
-    require(ids != nullptr, "ids must not be NULL.");
+    require(ids != nullptr || nq == 0, "ids must not be NULL.");
     host_rows(rows, n, bytes);
     host_rows(queries, nq, bytes);
     mlxvs_b200::hamming_knn(rows, n, queries, nq, bytes, k, ids, distances,
@@ -415,7 +415,7 @@ int mlxvs_knn_keys_device(const float* base, int64_t n, const float* queries, in
                           int32_t d, int32_t k, mlxvs_metric metric, int64_t id_offset,
                           uint64_t* keys, void* stream) {
   return guarded([&] {
-    require(keys != nullptr, "keys must not be NULL.");
+    require(keys != nullptr || nq == 0, "keys must not be NULL.");
     host_rows(base, n, d);
     host_rows(queries, nq, d);
     mlxvs_b200::knn_keys(base, n, queries, nq, d, k, to_metric(metric), id_offset, keys,
@@ -427,7 +427,7 @@ int mlxvs_hamming_keys_device(const uint8_t* rows, int64_t n, const uint8_t* que
                               int32_t bytes, int32_t k, int64_t id_offset, uint64_t* keys,
                               void* stream) {
   return guarded([&] {
-    require(keys != nullptr, "keys must not be NULL.");
+    require(keys != nullptr || nq == 0, "keys must not be NULL.");
     host_rows(rows, n, bytes);
     host_rows(queries, nq, bytes);
     mlxvs_b200::hamming_keys(rows, n, queries, nq, bytes, k, id_offset, keys,
@@ -442,6 +442,46 @@ int mlxvs_merge_keys_device(const uint64_t* lists, int32_t num_lists, int64_t nq
     mlxvs_b200::merge_keys(lists, num_lists, nq, k, kind, queries, d, ids, distances,
                            static_cast<cudaStream_t>(stream));
   });
+}
+
+int mlxvs_exchange_create(int32_t world, int32_t rank, int64_t capacity_keys,
+                          void** exchange) {
+  return guarded([&] {
+    require(exchange != nullptr, "exchange must not be NULL.");
+    *exchange = mlxvs_b200::exchange_create(world, rank, capacity_keys);
+  });
+}
+
+int mlxvs_exchange_handle(void* exchange, uint8_t* handle) {
+  return guarded([&] {
+    mlxvs_b200::exchange_handle(static_cast<mlxvs_b200::Exchange*>(exchange), handle);
+  });
+}
+
+int mlxvs_exchange_open(void* exchange, int32_t peer, const uint8_t* handle) {
+  return guarded([&] {
+    mlxvs_b200::exchange_open(static_cast<mlxvs_b200::Exchange*>(exchange), peer, handle);
+  });
+}
+
+int mlxvs_exchange_keys(void* exchange, uint32_t epoch, uint64_t** keys) {
+  return guarded([&] {
+    require(keys != nullptr, "keys must not be NULL.");
+    *keys = mlxvs_b200::exchange_keys(static_cast<mlxvs_b200::Exchange*>(exchange), epoch);
+  });
+}
+
+int mlxvs_exchange_merge_device(void* exchange, uint32_t epoch, int64_t nq, int32_t k,
+                                int32_t kind, const float* queries, int32_t d, int32_t* ids,
+                                float* distances, void* stream) {
+  return guarded([&] {
+    mlxvs_b200::exchange_merge(static_cast<mlxvs_b200::Exchange*>(exchange), epoch, nq, k, kind,
+                               queries, d, ids, distances, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int mlxvs_exchange_destroy(void* exchange) {
+  return guarded([&] { mlxvs_b200::exchange_destroy(static_cast<mlxvs_b200::Exchange*>(exchange)); });
 }
 
 int mlxvs_hamming_knn_noalloc(const uint8_t* rows, int64_t n, const uint8_t* queries,

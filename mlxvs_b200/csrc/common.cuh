@@ -56,6 +56,7 @@ enum : uint32_t {
   ERR_WAIT_PRODUCER = 1u,
   ERR_WAIT_MMA = 2u,
   ERR_WAIT_EPILOGUE = 4u,
+  ERR_WAIT_PEER = 8u,
 };
 
 #ifdef __CUDACC__

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -143,9 +144,14 @@ void profile_resolve_speculative(const char* kept_as) {
 // The flags of a call's prep read back through pinned memory: one buffer and
 // one event per (host thread, device), so a call waits for the copy alone
 // while the kernels enqueued after it keep running.
+// Pinned words the prep kernels' flags are copied into, on a stream of its
+// own: the copy waits for the preps (event `prepped`) but the kernels queued
+// after them on the caller's stream do not wait for the copy.
 struct FlagMailbox {
   uint32_t* host = nullptr;
   cudaEvent_t ev = nullptr;
+  cudaEvent_t prepped = nullptr;
+  cudaStream_t side = nullptr;
 };
 FlagMailbox& flag_mailbox() {
   thread_local FlagMailbox boxes[64];
@@ -158,6 +164,8 @@ FlagMailbox& flag_mailbox() {
   if (b.host == nullptr) {
     CK(cudaHostAlloc(reinterpret_cast<void**>(&b.host), 64, cudaHostAllocDefault));
     CK(cudaEventCreateWithFlags(&b.ev, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&b.prepped, cudaEventDisableTiming));
+    CK(cudaStreamCreateWithFlags(&b.side, cudaStreamNonBlocking));
   }
   return b;
 }
@@ -903,8 +911,10 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
   launch_prep(pb, dev.sms, s);
   launch_prep(pq, dev.sms, s);
   FlagMailbox& mb = flag_mailbox();
-  CK(cudaMemcpyAsync(mb.host, flags, 32, cudaMemcpyDeviceToHost, s));
-  CK(cudaEventRecord(mb.ev, s));
+  CK(cudaEventRecord(mb.prepped, s));
+  CK(cudaStreamWaitEvent(mb.side, mb.prepped, 0));
+  CK(cudaMemcpyAsync(mb.host, flags, 32, cudaMemcpyDeviceToHost, mb.side));
+  CK(cudaEventRecord(mb.ev, mb.side));
   // k <= 16 (register lists), L2 or inner product: the one-pass search on
   // exact operands (for L2 with -|b|^2 in the MMA) is launched before the
   // flags are read, so the GPU does not wait for the host; its CTAs return
@@ -1396,6 +1406,146 @@ void profile_read(const char* name, double* total_ms, int64_t* launches) {
   }
   if (total_ms) *total_ms = ms;
   if (launches) *launches = count;
+}
+
+// ------------------------------------------------------------ peer exchange
+// Buffer of one GPU: [flag: u32][failed: u32][pad to 256 B][slot 0 keys]
+// [slot 1 keys], from cudaMalloc (IPC handles need it).  The flag holds the
+// latest epoch whose keys are complete; failed, the epoch of a step whose
+// wait gave up.
+
+constexpr size_t EXCHANGE_HEADER = 256;
+// Ample for ranks that reach the merge within one step of each other: the
+// time limit guards against a rank that never comes, not against load
+// imbalance.
+constexpr uint64_t EXCHANGE_WAIT_NS = 10ull * 1000 * 1000 * 1000;
+
+struct Exchange {
+  int device = -1;
+  int world = 0;
+  int rank = 0;
+  int64_t capacity = 0;
+  uint8_t* own = nullptr;
+  uint8_t* peer[MERGE_MAX_PEERS] = {};
+  bool opened[MERGE_MAX_PEERS] = {};
+};
+
+namespace {
+uint64_t* slot_of(uint8_t* buf, int64_t capacity, uint32_t epoch) {
+  return reinterpret_cast<uint64_t*>(buf + EXCHANGE_HEADER) + (size_t)(epoch & 1u) * capacity;
+}
+}  // namespace
+
+Exchange* exchange_create(int world, int rank, int64_t capacity_keys) {
+  require(world >= 1 && world <= MERGE_MAX_PEERS,
+          "[mlxvs::exchange] world must be in [1, " + std::to_string(MERGE_MAX_PEERS) + "].");
+  require(rank >= 0 && rank < world, "[mlxvs::exchange] rank must be in [0, world).");
+  require(capacity_keys >= 1, "[mlxvs::exchange] capacity must be at least 1 key.");
+  device_info();
+  auto x = std::make_unique<Exchange>();
+  CK(cudaGetDevice(&x->device));
+  x->world = world;
+  x->rank = rank;
+  x->capacity = capacity_keys;
+  const size_t bytes = EXCHANGE_HEADER + 2 * (size_t)capacity_keys * sizeof(uint64_t);
+  CK(cudaMalloc(&x->own, bytes));
+  CK(cudaMemset(x->own, 0, bytes));
+  x->peer[rank] = x->own;
+  x->opened[rank] = true;
+  return x.release();
+}
+
+void exchange_handle(Exchange* x, void* handle) {
+  require(x != nullptr && handle != nullptr, "[mlxvs::exchange] null argument.");
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, x->own));
+  std::memcpy(handle, &h, sizeof(h));
+}
+
+void exchange_open(Exchange* x, int peer, const void* handle) {
+  require(x != nullptr && handle != nullptr, "[mlxvs::exchange] null argument.");
+  require(peer >= 0 && peer < x->world, "[mlxvs::exchange] peer must be in [0, world).");
+  if (peer == x->rank || x->opened[peer]) return;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  x->peer[peer] = static_cast<uint8_t*>(p);
+  x->opened[peer] = true;
+}
+
+uint64_t* exchange_keys(Exchange* x, uint32_t epoch) {
+  require(x != nullptr, "[mlxvs::exchange] null exchange.");
+  require(epoch >= 1, "[mlxvs::exchange] epochs start at 1.");
+  return slot_of(x->own, x->capacity, epoch);
+}
+
+void exchange_merge(Exchange* x, uint32_t epoch, int64_t nq, int k, int kind,
+                    const float* queries, int d, int32_t* ids, float* dist, cudaStream_t s) {
+  require(x != nullptr, "[mlxvs::exchange] null exchange.");
+  require(epoch >= 1, "[mlxvs::exchange] epochs start at 1.");
+  require(k >= 1 && merge_quad_fits(x->world, k),
+          "[mlxvs::exchange] k must be in [1, 32] with world * k <= " +
+              std::to_string(MERGE_QUAD_MAX) + ".");
+  require(nq >= 0 && nq * k <= x->capacity, "[mlxvs::exchange] nq * k exceeds the capacity.");
+  require(kind >= 0 && kind <= KIND_HAMMING, "[mlxvs::exchange] unknown kind.");
+  require(ids != nullptr || nq == 0, "[mlxvs::exchange] ids must not be NULL.");
+  require(kind != static_cast<int>(Metric::L2) || nq == 0 || (queries != nullptr && d >= 1),
+          "[mlxvs::exchange] L2 distances need the queries [nq, d].");
+  for (int r = 0; r < x->world; ++r)
+    require(x->opened[r], "[mlxvs::exchange] peer " + std::to_string(r) + " is not opened.");
+  int cur = -1;
+  CK(cudaGetDevice(&cur));
+  require(cur == x->device, "[mlxvs::exchange] the current device is not the exchange's.");
+  DeviceInfo& dev = device_info();
+  // every step publishes and waits, also with no queries, so that the GPUs'
+  // epochs stay in step
+  ExchangeFlags f{};
+  f.own = reinterpret_cast<volatile uint32_t*>(x->own);
+  for (int r = 0; r < x->world; ++r) f.flag[r] = reinterpret_cast<volatile uint32_t*>(x->peer[r]);
+  f.world = x->world;
+  f.epoch = epoch;
+  f.failed = reinterpret_cast<uint32_t*>(x->own) + 1;
+  f.err = dev.err;
+  f.limit_cycles = (long long)(2 * EXCHANGE_WAIT_NS);
+  {
+    ProfScope prof("exchange_wait", s);
+    exchange_wait_kernel<<<1, 32, 0, s>>>(f);
+    CK(cudaGetLastError());
+  }
+  if (nq == 0) return;
+  PeerLists pl{};
+  for (int r = 0; r < x->world; ++r) pl.p[r] = slot_of(x->peer[r], x->capacity, epoch);
+  pl.failed = f.failed;
+  pl.epoch = epoch;
+  ProfScope prof("merge", s);
+  const unsigned blocks = (unsigned)((nq + 7) / 8);
+  const size_t smem = (size_t)x->world * k * 8 * sizeof(uint64_t);
+  const float* qrows = kind == static_cast<int>(Metric::L2) ? queries : nullptr;
+#define MLXVS_MERGE_PEERS(KR_)                                                           \
+  merge_keys_quad_kernel<KR_, true><<<blocks, 32, smem, s>>>(                          \
+      nullptr, x->world, nq, nq, k, kind, nullptr, nullptr, ids, dist, 1.0f, qrows, d, pl)
+  if (k <= 10)
+    MLXVS_MERGE_PEERS(10);
+  else if (k <= 16)
+    MLXVS_MERGE_PEERS(16);
+  else
+    MLXVS_MERGE_PEERS(32);
+#undef MLXVS_MERGE_PEERS
+  CK(cudaGetLastError());
+}
+
+void exchange_destroy(Exchange* x) {
+  if (x == nullptr) return;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != x->device) cudaSetDevice(x->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < x->world; ++r)
+    if (r != x->rank && x->opened[r] && x->peer[r]) cudaIpcCloseMemHandle(x->peer[r]);
+  cudaFree(x->own);
+  if (cur >= 0 && cur != x->device) cudaSetDevice(cur);
+  delete x;
 }
 
 const char* version() { return MLXVS_B200_VERSION; }

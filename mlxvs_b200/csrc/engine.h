@@ -89,6 +89,29 @@ void profile_issued(const char* name, double* ops);
 void hamming_knn_noalloc(const uint8_t* rows, int64_t n, const uint8_t* queries, int64_t nq,
                          int bytes, int k, int32_t* ids, float* dist, cudaStream_t s);
 
+/** A row-sharded search's exchange of key lists between the GPUs of one
+ * node, replacing an all-gather followed by a merge: every GPU writes its
+ * [nq, k] keys of a step into its own buffer, publishes the step's epoch in
+ * a flag there, and merges the world's lists by reading its peers' buffers
+ * over NVLink (CUDA IPC mappings, plain loads).  Two key slots alternate by
+ * epoch, so a GPU never overwrites keys a slower peer may still read.  One
+ * object per process and GPU; epochs start at 1 and rise by one per step,
+ * in the same order on every GPU. */
+struct Exchange;
+Exchange* exchange_create(int world, int rank, int64_t capacity_keys);
+/** The IPC handle (64 bytes) of this GPU's buffer, for the peers. */
+void exchange_handle(Exchange* x, void* handle);
+/** Maps a peer's buffer from its handle. */
+void exchange_open(Exchange* x, int peer, const void* handle);
+/** This GPU's key slot of an epoch: [nq, k] keys, nq * k <= capacity. */
+uint64_t* exchange_keys(Exchange* x, uint32_t epoch);
+/** Publishes this GPU's keys of the epoch, waits (bounded) for every peer's,
+ * and merges the world's lists into ids and distances of the given kind, as
+ * merge_keys does; queued on s. */
+void exchange_merge(Exchange* x, uint32_t epoch, int64_t nq, int k, int kind,
+                    const float* queries, int d, int32_t* ids, float* dist, cudaStream_t s);
+void exchange_destroy(Exchange* x);
+
 /** Version string. */
 const char* version();
 

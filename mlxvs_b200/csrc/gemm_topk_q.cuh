@@ -45,9 +45,10 @@
 //
 // Queue protocol (single producer, single consumer per (column half, query)):
 // the filter lane writes the chunk's 16 scores and first column into slot
-// tail % QD, fences, then advances tail; the select lane reads tail, fences,
-// reads the slot, and advances head once done with it.  A chunk with column
-// -1 marks the end of the filter lane's unit.  Every wait is bounded.
+// tail % QD, then advances tail with a release store; the select lane reads
+// tail with an acquire load, reads the slot, and advances head with a
+// release store once done with it.  A chunk with column -1 marks the end of
+// the filter lane's unit.  Every wait is bounded.
 #pragma once
 
 #include "gemm_topk.cuh"
@@ -120,6 +121,27 @@ __device__ __forceinline__ long long qk_cycle_limit(uint64_t limit_ns) {
   return (long long)(2 * limit_ns);
 }
 
+// Queue counters in shared memory with CTA-scope acquire / release order:
+// the consumer's read of tail orders its reads of the slot after it, the
+// producer's write of tail orders its writes of the slot before it, and the
+// consumer's write of head orders its reads of the slot before it (cheaper
+// than a full CTA fence around plain accesses).
+__device__ __forceinline__ uint32_t qk_ld_acquire(const volatile uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];"
+               : "=r"(v)
+               : "r"((uint32_t)__cvta_generic_to_shared(const_cast<const uint32_t*>(p)))
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void qk_st_release(volatile uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(const_cast<uint32_t*>(p))),
+               "r"(v)
+               : "memory");
+}
+
 // Copies one 16-score chunk into this lane's queue of its column half.
 // Returns false when the wait for a free slot gave up (abort raised, or the
 // time limit passed).
@@ -144,8 +166,7 @@ __device__ __forceinline__ bool qk_push(const float* v, int32_t col, float4* qs,
       dst[j4 * QK_QB] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
   }
   qc[slot * QK_QB] = col;
-  __threadfence_block();
-  *tail_p = ++tail;
+  qk_st_release(tail_p, ++tail);
   return true;
 }
 
@@ -638,7 +659,9 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
     // ------------------------------------------------------------- select
     const int rg = warp - QK_FILTER_WARPS;
     const int row = rg * 32 + lane;
-    uint32_t head[2] = {0u, 0u};
+    // consumed chunks per column half's queue (two scalars: an array indexed
+    // by the runtime half would live in local memory)
+    uint32_t head0 = 0u, head1 = 0u;
     uint64_t key[KR > 0 ? KR : 1];
     uint32_t uidx = 0;
     bool ok = true;
@@ -692,14 +715,15 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
 #pragma unroll
         for (int tr = 0; tr < 2; ++tr) {
           const uint32_t c = pref ^ (uint32_t)tr;
-          if (!got && !((ended >> c) & 1u) && qtail[c * QB + row] != head[c]) {
-            __threadfence_block();
-            const uint32_t slot = head[c] % (uint32_t)QD;
+          const uint32_t hc = c ? head1 : head0;
+          if (!got && !((ended >> c) & 1u) && qk_ld_acquire(qtail + c * QB + row) != hc) {
+            const uint32_t slot = hc % (uint32_t)QD;
             const int32_t col = qcol[(c * QD + slot) * QB + row];
             got = true;
             if (col < 0) {
               ended |= 1u << c;
-              qhead[c * QB + row] = ++head[c];
+              if (c) head1 = hc + 1u; else head0 = hc + 1u;
+              qk_st_release(qhead + c * QB + row, hc + 1u);
             } else {
               const float4* src = qscore + ((size_t)(c * QD + slot) * 4) * QB + row;
 #pragma unroll
@@ -716,8 +740,8 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
               ent = c * QD + slot;
               ech = c;
               if (mask == 0) {
-                __threadfence_block();
-                qhead[c * QB + row] = ++head[c];
+                if (c) head1 = hc + 1u; else head0 = hc + 1u;
+                qk_st_release(qhead + c * QB + row, hc + 1u);
               }
             }
             pref = c ^ 1u;
@@ -751,8 +775,9 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
               }
             }
             if (mask == 0) {
-              __threadfence_block();
-              qhead[ech * QB + row] = ++head[ech];
+              const uint32_t nh = (ech ? head1 : head0) + 1u;
+              if (ech) head1 = nh; else head0 = nh;
+              qk_st_release(qhead + ech * QB + row, nh);
             }
           }
         }

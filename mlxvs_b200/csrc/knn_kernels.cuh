@@ -584,6 +584,24 @@ __device__ __forceinline__ void merge_write(uint64_t key, int64_t q, int o, int 
   }
 }
 
+// The lists of a merge whose lists live on different GPUs of the node (the
+// row shards' keys, each in its GPU's exchange buffer, read over NVLink):
+// list l is p[l] [nq][k].  failed holds the epoch of a step whose peer keys
+// never arrived; that step's merge writes missing results instead of
+// reading stale ones.
+constexpr int MERGE_MAX_PEERS = 8;
+struct PeerLists {
+  const uint64_t* p[MERGE_MAX_PEERS];
+  const volatile uint32_t* failed;
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* a) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
 // Whether merge_keys_quad_kernel takes a merge of num_lists lists of k keys.
 __host__ __device__ inline bool merge_quad_fits(int64_t num_lists, int k) {
   return k <= 32 && num_lists <= 32 && num_lists * k <= MERGE_QUAD_MAX;
@@ -604,25 +622,36 @@ __host__ __device__ inline bool merge_quad_fits(int64_t num_lists, int k) {
 // (list_insert), skipping a key it already holds.  For L2 distances the
 // kernel takes |q|^2 from qq, or computes it from queries [nq, d] when qq is
 // null.
-template <int KR>
+// With PEERS the lists are peers.p[l] (other GPUs' memory, read with
+// system-scope loads, which no cache of this GPU answers from an older step).
+template <int KR, bool PEERS = false>
 __global__ void __launch_bounds__(32)
     merge_keys_quad_kernel(const uint64_t* __restrict__ lists, int32_t num_lists,
                            int64_t list_rows, int64_t nq, int32_t k, int32_t kind,
                            const float* __restrict__ qq, uint64_t* __restrict__ out_keys,
                            int32_t* __restrict__ ids, float* __restrict__ dist, float scale,
-                           const float* __restrict__ queries, int32_t d) {
+                           const float* __restrict__ queries, int32_t d,
+                           const PeerLists peers = {}) {
   extern __shared__ __align__(16) uint64_t stage[];  // [num_lists][8][k]
   const int lane = threadIdx.x;
   const int64_t q0 = (int64_t)blockIdx.x * 8;
   const int rows = (int)(nq - q0 < 8 ? nq - q0 : 8);
   const int per_list = rows * k;
+  bool lost = false;
+  if constexpr (PEERS) lost = *peers.failed == peers.epoch;
   for (int l = 0; l < num_lists; ++l) {
-    const uint64_t* src = lists + ((size_t)l * list_rows + q0) * k;
-    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(stage + (size_t)l * 8 * k);
-    for (int i = lane; i < per_list; i += 32)
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst + 8u * (uint32_t)i),
-                   "l"(src + i)
-                   : "memory");
+    if constexpr (PEERS) {
+      const uint64_t* src = peers.p[l] + (size_t)q0 * k;
+      uint64_t* dst = stage + (size_t)l * 8 * k;
+      for (int i = lane; i < per_list; i += 32) dst[i] = lost ? 0ull : ld_relaxed_sys(src + i);
+    } else {
+      const uint64_t* src = lists + ((size_t)l * list_rows + q0) * k;
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(stage + (size_t)l * 8 * k);
+      for (int i = lane; i < per_list; i += 32)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst + 8u * (uint32_t)i),
+                     "l"(src + i)
+                     : "memory");
+    }
   }
   // L2 without qq: |q|^2 of the warp's queries [nq, d] while the copies
   // land, in row_sumsq_kernel's order (lane-strided sums, then warp_sum)
@@ -729,6 +758,50 @@ __global__ void __launch_bounds__(32)
   for (int i = 0; i < KR; ++i) {
     if (i >= k) break;
     merge_write(key[i], q, k - 1 - i, k, kind, qn, scale, out_keys, ids, dist);
+  }
+}
+
+// The flags of one exchange step across the node's GPUs: this GPU's flag
+// and every GPU's (peers' over NVLink), the step's epoch, and where a wait
+// that gave up is recorded.
+struct ExchangeFlags {
+  volatile uint32_t* own;
+  const volatile uint32_t* flag[MERGE_MAX_PEERS];
+  int32_t world;
+  uint32_t epoch;
+  uint32_t* failed;
+  uint32_t* err;
+  long long limit_cycles;
+};
+
+// Publishes this GPU's keys of the epoch (written by the kernels before this
+// one on the stream) and waits until every GPU has published its own: lane
+// r polls GPU r's flag.  A wait that runs past the limit marks the step
+// failed and raises ERR_WAIT_PEER instead of hanging.
+__global__ void __launch_bounds__(32) exchange_wait_kernel(ExchangeFlags f) {
+  const int lane = threadIdx.x;
+  if (lane == 0) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.own), "r"(f.epoch) : "memory");
+  }
+  __syncwarp();
+  bool ok = true;
+  if (lane < f.world) {
+    const long long start = clock64();
+    for (uint32_t i = 0;; ++i) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f.flag[lane]) : "memory");
+      if ((int32_t)(v - f.epoch) >= 0) break;
+      if ((i & 15u) == 15u && clock64() - start > f.limit_cycles) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0) {
+    *f.failed = f.epoch;
+    atomicOr(f.err, ERR_WAIT_PEER);
   }
 }
 

@@ -124,3 +124,16 @@ def test_no_gpu_fails_loudly(lib):
     assert b"CUDA" in lib.mlxvs_last_error()
     with pytest.raises(RuntimeError):
         mv.brute_force_knn(b, b[:2], 3)
+
+
+def test_exchange_argument_errors(lib):
+    # the peer exchange's set-up checks its arguments before any CUDA call
+    p = ctypes.c_void_p()
+    assert lib.mlxvs_exchange_create(9, 0, 100, ctypes.byref(p)) == 1
+    assert b"world must be in [1, 8]" in lib.mlxvs_last_error()
+    assert lib.mlxvs_exchange_create(2, 2, 100, ctypes.byref(p)) == 1
+    assert lib.mlxvs_exchange_create(2, 0, 0, ctypes.byref(p)) == 1
+    assert lib.mlxvs_exchange_create(2, 0, 100, None) == 1
+    assert lib.mlxvs_exchange_keys(None, 1, ctypes.byref(p)) == 1
+    assert lib.mlxvs_exchange_merge_device(None, 1, 10, 10, 1, None, 0, None, None, None) == 1
+    assert lib.mlxvs_exchange_destroy(None) == 0

@@ -87,6 +87,39 @@ def _worker(rank, world, port, out):
         side.synchronize()
         out[(rank, "stream")] = bool(torch.equal(got[0], want[0]) and
                                      torch.equal(got[1], want[1]))
+        # the peer exchange (lists read from the other GPU's memory) gives
+        # the NCCL path's results, step after step (the two key slots
+        # alternate), also for a step with no queries and for Hamming codes
+        ex = mvd.PeerExchange(1_000 * 32)
+        okx = True
+        for metric, k, integer in CASES:
+            if not ex.fits(1_000, k):
+                continue
+            b, q = make_case(metric, integer)
+            bounds = mvd.shard_bounds(b.shape[0], world)
+            lo, hi = bounds[rank], bounds[rank + 1]
+            shard = torch.from_numpy(b[lo:hi]).to(dev)
+            tq = torch.from_numpy(q).to(dev)
+            want = mvd.sharded_brute_force_knn(shard, tq, k, metric, id_offset=lo)
+            for _ in range(3):
+                got = mvd.sharded_brute_force_knn(shard, tq, k, metric, id_offset=lo, exchange=ex)
+                okx &= bool(torch.equal(got[0], want[0]) and torch.equal(got[1], want[1]))
+            empty = mvd.sharded_brute_force_knn(shard, tq[:0], k, metric, id_offset=lo,
+                                                exchange=ex)
+            okx &= tuple(empty[0].shape) == (0, k)
+        codes, qc = data.hamming_codes(40_000, 128, 64, 0.1, seed=45, nq=500)
+        bounds = mvd.shard_bounds(codes.shape[0], world)
+        lo, hi = bounds[rank], bounds[rank + 1]
+        tcodes = torch.from_numpy(codes[lo:hi]).to(dev)
+        tqc = torch.from_numpy(qc).to(dev)
+        want = mvd.sharded_hamming_knn(tcodes, tqc, 10, id_offset=lo)
+        got = mvd.sharded_hamming_knn(tcodes, tqc, 10, id_offset=lo, exchange=ex)
+        okx &= bool(torch.equal(got[0], want[0]) and torch.equal(got[1], want[1]))
+        mv.synchronize()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ex.close()
+        out[(rank, "exchange")] = okx
         # the k-NN graph split by rows (all rows on every rank, no exchange
         # but the final gather)
         x, _ = data.gaussian_mixture_int(20_001, 64, 16, seed=44)
@@ -117,6 +150,7 @@ def test_two_gpus_match_single():
     for r in range(WORLD):
         assert res[(r, "allnn")], r
         assert res[(r, "stream")], r
+        assert res[(r, "exchange")], r
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
@@ -142,3 +176,36 @@ def test_stream_argument_one_rank():
                                              stream=side.cuda_stream)
     side.synchronize()
     assert torch.equal(ids2, want[0]) and torch.equal(dst2, want[1])
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_peer_exchange_one_rank():
+    # the exchange's kernels with one GPU (no process group): the wait sees
+    # this GPU's own flag, the merge reads this GPU's slot; several epochs
+    # (both slots), sizes and kinds, against the plain search
+    import mlxvs_b200 as mv
+    from mlxvs_b200 import distributed as mvd
+
+    dev = torch.device("cuda", 0)
+    b, _ = data.gaussian_mixture_int(50_000, 128, 32, seed=46)
+    tb = torch.from_numpy(b).to(dev)
+    ex = mvd.PeerExchange(2_000 * 32)
+    try:
+        for i, (nq, k, metric) in enumerate([(700, 10, "l2"), (2_000, 32, "inner_product"),
+                                             (0, 10, "l2"), (1_999, 16, "l2")]):
+            _, q = data.gaussian_mixture_int(10, 128, 32, seed=50 + i, nq=max(nq, 1))
+            tq = torch.from_numpy(q[:nq]).to(dev)
+            ids, dst = mvd.sharded_brute_force_knn(tb, tq, k, metric, id_offset=0, exchange=ex)
+            want = mv.brute_force_knn(tb, tq, k, metric)
+            assert torch.equal(ids, want[0]) and torch.equal(dst, want[1]), (nq, k, metric)
+            assert ex.epoch == i + 1
+        assert not ex.fits(2_000, 33) and not ex.fits(3_000, 32)
+        codes, qc = data.hamming_codes(20_000, 64, 32, 0.1, seed=47, nq=300)
+        got = mvd.sharded_hamming_knn(torch.from_numpy(codes).to(dev),
+                                      torch.from_numpy(qc).to(dev), 10, id_offset=0, exchange=ex)
+        want = mv.hamming_knn(codes, qc, 10)
+        assert np.array_equal(got[0].cpu().numpy(), want[0])
+        assert np.array_equal(got[1].cpu().numpy(), want[1])
+        mv.synchronize()
+    finally:
+        ex.close()
