@@ -637,6 +637,9 @@ def main():
     if rank == 0 and not args.no_parity and not emulated:
         parity = check_parity(w, full_base, q, ids, dist_out, k, metric)
     # e2e: the public API on host (pinned) buffers, copies inside the region
+    # (every rank starts it together: rank 0 may have spent seconds on the
+    # parity check, and a peer exchange waits for all ranks)
+    barrier()
     e2e = None
     if args.e2e_steps > 0:
         base_h = shard.cpu().pin_memory()

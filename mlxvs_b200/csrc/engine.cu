@@ -1418,7 +1418,7 @@ constexpr size_t EXCHANGE_HEADER = 256;
 // Ample for ranks that reach the merge within one step of each other: the
 // time limit guards against a rank that never comes, not against load
 // imbalance.
-constexpr uint64_t EXCHANGE_WAIT_NS = 10ull * 1000 * 1000 * 1000;
+constexpr uint64_t EXCHANGE_WAIT_NS = 30ull * 1000 * 1000 * 1000;
 
 struct Exchange {
   int device = -1;
