@@ -258,6 +258,33 @@ __device__ __forceinline__ void list_insert(uint64_t (&key)[KR], uint64_t x) {
   }
 }
 
+// Inserts two keys x >= y at once (y = 0: none) into the same list, keeping
+// the KR best of the list and both.  In the merged ascending order y sits
+// at #(keys < y) and x at #(keys < x) + 1; slot i of the result is the
+// (i + 2)-th smallest of the union, so it takes key[i + 2] (both below it),
+// y, key[i + 1] (only y below), x, or keeps key[i].
+template <int KR>
+__device__ __forceinline__ void list_insert2(uint64_t (&key)[KR], uint64_t x, uint64_t y) {
+  bool bx[KR], by[KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    bx[i] = x > key[i];
+    by[i] = y > key[i];
+  }
+  uint64_t n[KR];
+#pragma unroll
+  for (int i = 0; i < KR; ++i) {
+    const bool by1 = i + 1 < KR ? by[i + 1] : false;
+    const bool by2 = i + 2 < KR ? by[i + 2] : false;
+    const bool bx1 = i + 1 < KR ? bx[i + 1] : false;
+    const uint64_t k1 = i + 1 < KR ? key[i + 1] : 0ull;
+    const uint64_t k2 = i + 2 < KR ? key[i + 2] : 0ull;
+    n[i] = by1 ? (by2 ? k2 : y) : (bx[i] ? (bx1 ? k1 : x) : key[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < KR; ++i) key[i] = n[i];
+}
+
 // The register lists' slow path for 16 scores v[0..15] of columns col0..:
 // every lane calls it (the votes are warp-wide); `mine` marks the lanes with
 // a score at or above their floor.  Each such lane marks those scores in a

@@ -16,9 +16,10 @@
 //   select warps 8..11  warp 8 + r owns queries 32 r .. 32 r + 31, one per
 //                       lane, and holds each query's k best keys as one
 //                       sorted register list covering both column halves.
-//                       Every lane takes the next chunk of its query's
-//                       queues, and the warp inserts the chunks' candidates
-//                       (one per lane per step, all lanes at once); the
+//                       Every lane takes the next chunk of each of its
+//                       query's two queues, and the warp inserts the chunks'
+//                       candidates (two per lane per round, all lanes at
+//                       once, one merge network for the pair); the
 //                       list's worst key is the query's floor, published to
 //                       the filter warps and the relay warp through shared
 //                       memory.
@@ -706,24 +707,24 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
         cbuf1 = p.collect + (((size_t)split * 2 + 1) * p.nq_pad + q) * (size_t)p.collect_cap;
       }
       uint32_t ended = 0;  // bit c: the end marker of column half c was seen
-      uint32_t pref = 0;
       long long idle_since = 0;
       for (;;) {
-        // each lane takes at most one chunk of its query's queues
-        uint32_t mask = 0, id0 = 0, ent = 0, ech = 0;
+        // each lane takes the next chunk of each of its query's two queues
+        // (c static in the unrolled loop, so the per-half values stay in
+        // registers)
+        const uint64_t floor_before = floor;
+        uint32_t mk[2] = {0u, 0u}, idb[2] = {0u, 0u}, en[2] = {0u, 0u};
         bool got = false;
 #pragma unroll
-        for (int tr = 0; tr < 2; ++tr) {
-          const uint32_t c = pref ^ (uint32_t)tr;
+        for (int c = 0; c < 2; ++c) {
           const uint32_t hc = c ? head1 : head0;
-          if (!got && !((ended >> c) & 1u) && qk_ld_acquire(qtail + c * QB + row) != hc) {
+          if (!((ended >> c) & 1u) && qk_ld_acquire(qtail + c * QB + row) != hc) {
             const uint32_t slot = hc % (uint32_t)QD;
             const int32_t col = qcol[(c * QD + slot) * QB + row];
             got = true;
+            uint32_t mask = 0;
             if (col < 0) {
               ended |= 1u << c;
-              if (c) head1 = hc + 1u; else head0 = hc + 1u;
-              qk_st_release(qhead + c * QB + row, hc + 1u);
             } else {
               const float4* src = qscore + ((size_t)(c * QD + slot) * 4) * QB + row;
 #pragma unroll
@@ -736,48 +737,64 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
               }
               const int64_t valid = p.n_valid - (int64_t)col;
               if (valid < 16) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
-              id0 = (uint32_t)(p.id_offset + col);
-              ent = c * QD + slot;
-              ech = c;
-              if (mask == 0) {
-                if (c) head1 = hc + 1u; else head0 = hc + 1u;
-                qk_st_release(qhead + c * QB + row, hc + 1u);
-              }
+              idb[c] = (uint32_t)(p.id_offset + col);
+              en[c] = c * QD + slot;
             }
-            pref = c ^ 1u;
+            mk[c] = mask;
+            if (mask == 0) {
+              if (c) head1 = hc + 1u; else head0 = hc + 1u;
+              qk_st_release(qhead + c * QB + row, hc + 1u);
+            }
           }
         }
-        // insert (or collect) the chunks' candidates, one per lane per step
-        const uint64_t floor_before = floor;
-        while (__any_sync(0xffffffffu, mask != 0)) {
-          if (mask) {
-            const int j = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const float vj = reinterpret_cast<const float*>(
-                qscore + ((size_t)ent * 4 + (j >> 2)) * QB + row)[j & 3];
-            const uint32_t id = id0 + (uint32_t)j;
-            const uint64_t x = make_key(vj, id);
-            if (x > floor && id != self_id) {
+        // insert (or collect) the chunks' candidates: each round a lane
+        // takes the next two marked scores (half 0's first), all lanes at
+        // once; a chunk's slot is released once its last mark is taken
+        while (__any_sync(0xffffffffu, (mk[0] | mk[1]) != 0u)) {
+          uint64_t cand[2] = {0ull, 0ull};
+#pragma unroll
+          for (int t = 0; t < (MODE == 0 ? 2 : 1); ++t) {
+            if (mk[0] | mk[1]) {
+              const uint32_t h = mk[0] ? 0u : 1u;
+              const uint32_t m = h ? mk[1] : mk[0];
+              const int j = __ffs(m) - 1;
+              const uint32_t rest = m & (m - 1);
+              if (h) mk[1] = rest; else mk[0] = rest;
+              const uint32_t e = h ? en[1] : en[0];
+              const float vj = reinterpret_cast<const float*>(
+                  qscore + ((size_t)e * 4 + (j >> 2)) * QB + row)[j & 3];
+              const uint32_t id = (h ? idb[1] : idb[0]) + (uint32_t)j;
+              const uint64_t x = make_key(vj, id);
+              const bool take = x > floor && id != self_id;
               if constexpr (MODE == 1) {
-                if (ech == 0) {
-                  if (cnt0 < p.collect_cap && cbuf0) cbuf0[cnt0] = x;
-                  ++cnt0;
-                } else {
-                  if (cnt1 < p.collect_cap && cbuf1) cbuf1[cnt1] = x;
-                  ++cnt1;
+                if (take) {
+                  if (h == 0) {
+                    if (cnt0 < p.collect_cap && cbuf0) cbuf0[cnt0] = x;
+                    ++cnt0;
+                  } else {
+                    if (cnt1 < p.collect_cap && cbuf1) cbuf1[cnt1] = x;
+                    ++cnt1;
+                  }
                 }
               } else {
-                list_insert<KR>(key, x);
-                if (key[0] > floor) {
-                  floor = key[0];
-                  thr = key_score(floor);
-                }
+                cand[t] = take ? x : 0ull;
+              }
+              if (rest == 0u) {
+                const uint32_t nh = (h ? head1 : head0) + 1u;
+                if (h) head1 = nh; else head0 = nh;
+                qk_st_release(qhead + h * QB + row, nh);
               }
             }
-            if (mask == 0) {
-              const uint32_t nh = (ech ? head1 : head0) + 1u;
-              if (ech) head1 = nh; else head0 = nh;
-              qk_st_release(qhead + ech * QB + row, nh);
+          }
+          if constexpr (MODE == 0) {
+            const uint64_t hi = cand[0] > cand[1] ? cand[0] : cand[1];
+            const uint64_t lo = cand[0] > cand[1] ? cand[1] : cand[0];
+            if (hi != 0ull) {
+              list_insert2<KR>(key, hi, lo);
+              if (key[0] > floor) {
+                floor = key[0];
+                thr = key_score(floor);
+              }
             }
           }
         }
