@@ -68,6 +68,21 @@ constexpr int QK_QB = 128;                                       // queries per 
 // within two tiles of each other through the MMA's accumulators), so a ring
 // of 8 per-unit counters (QD <= 4) tells the last of them apart.
 constexpr int QK_END_RING = 8;
+// A select warp with nothing queued sleeps between polls, from QK_NAP_MIN_NS
+// doubling up to QK_NAP_MAX_NS: each poll is a few dozen instructions issued
+// on an SM sub-partition that it shares with two filter warps and, on two of
+// the four, with the TMA or the MMA warp, whose issue latency the tensor
+// core feels directly.
+#ifndef MLXVS_QK_NAP_MAX_NS
+#define MLXVS_QK_NAP_MAX_NS 1024
+#endif
+constexpr uint32_t QK_NAP_MIN_NS = 32;
+constexpr uint32_t QK_NAP_MAX_NS = MLXVS_QK_NAP_MAX_NS;
+// The floor relay warp's interval between rounds.
+#ifndef MLXVS_QK_RELAY_NAP_NS
+#define MLXVS_QK_RELAY_NAP_NS 200
+#endif
+constexpr uint32_t QK_RELAY_NAP_NS = MLXVS_QK_RELAY_NAP_NS;
 
 // Shared-memory layout of the queued kernel, computed identically on host
 // and device.  The |b|^2 pieces of a tile travel with its first K chunk into
@@ -617,32 +632,28 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
         const uint32_t taddr =
             tmem_base + ((uint32_t)(rg * 32) << 16) + acc * GT_BN + (uint32_t)(ch * CW);
         const int32_t col_base = (int32_t)((int64_t)t * p.tile_stride * GT_BN + ch * CW);
+        // 64 columns per round trip to TMEM: two loads in flight, one wait
+        // (a wait for each 32 columns would put four load latencies, not
+        // two, on the path that frees the accumulator)
         uint32_t ra[32], rb[32];
-        tmem_ld32(taddr, ra);
-        tmem_wait_ld_regs(ra);
         const float* nbt = p.nb + (int64_t)t * p.tile_stride * GT_BN + ch * CW;
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
+          tmem_ld32(taddr + c * 32, ra);
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          qk_filter32<NBM, OP, QD>(ra, nbt + c * 32, col_base + c * 32, thr, p.dot_offset, qs,
-                                   qc, tail_p, head_p, tail, ok, abort_flag, p.wait_ns);
-          __syncwarp();
-          tmem_wait_ld_regs(rb);
-          if (c + 2 < NCH) {
-            tmem_ld32(taddr + (c + 2) * 32, ra);
-          } else {
+          tmem_wait_ld_regs(ra);
+          tmem_regs_ready(rb);
+          if (c + 2 >= NCH) {
             // the accumulator is free once its last columns are in registers
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
+          qk_filter32<NBM, OP, QD>(ra, nbt + c * 32, col_base + c * 32, thr, p.dot_offset, qs,
+                                   qc, tail_p, head_p, tail, ok, abort_flag, p.wait_ns);
           qk_filter32<NBM, OP, QD>(rb, nbt + c * 32 + 32, col_base + c * 32 + 32, thr,
                                    p.dot_offset, qs, qc, tail_p, head_p, tail, ok, abort_flag,
                                    p.wait_ns);
-          if (c + 2 < NCH) {
-            __syncwarp();
-            tmem_wait_ld_regs(ra);
-          }
         }
         ok = __all_sync(0xffffffffu, ok);
         acc ^= 1;
@@ -708,6 +719,7 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
       }
       uint32_t ended = 0;  // bit c: the end marker of column half c was seen
       long long idle_since = 0;
+      uint32_t nap = QK_NAP_MIN_NS;  // idle poll interval, doubled while nothing arrives
       for (;;) {
         // each lane takes the next chunk of each of its query's two queues
         // (c static in the unrolled loop, so the per-half values stay in
@@ -824,9 +836,11 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
             ok = false;
             break;
           }
-          __nanosleep(32);
+          __nanosleep(nap);
+          nap = nap * 2u < (uint32_t)QK_NAP_MAX_NS ? nap * 2u : (uint32_t)QK_NAP_MAX_NS;
         } else {
           idle_since = 0;
+          nap = QK_NAP_MIN_NS;
         }
       }
       if (!ok) break;
@@ -906,7 +920,7 @@ __global__ void __launch_bounds__(QK_THREADS, 1)
           ok = false;
           break;
         }
-        __nanosleep(200);
+        __nanosleep(QK_RELAY_NAP_NS);
       }
     }
   }
