@@ -960,37 +960,55 @@ void knn_core(const float* base, int64_t n, const float* queries, int64_t nq, in
       return std::max(-60, std::min(60, 14 - std::ilogb(amax)));
     };
     const int eb = scale_exp(amax_b), eq = scale_exp(amax_q);
-    const float sb = std::ldexp(1.0f, eb), sq = std::ldexp(1.0f, eq);
     if (n_pad / GT_BN >= 64) {
       // one fp16 pass of the scaled operands (hi only), every candidate
       // within twice its error bound of a sampled floor kept, then exact
       // float32 scores; the three-pass split below when buffers overflow
-      PrepParams pb1{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, nullptr,
-                     nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr, nullptr,
-                     nullptr};
-      PrepParams pq1{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, sq, q_hi,
-                     nullptr, nullptr, 0.0f, 0.0f, nullptr, nullptr, nullptr};
-      launch_prep(pb1, dev.sms, s);
-      launch_prep(pq1, dev.sms, s);
       float nb2, nq2;
       std::memcpy(&nb2, &hflags[5], 4);
       std::memcpy(&nq2, &hflags[6], 4);
       // |fp16 dot - exact dot| <= (2u + u^2 + (d + 16) 2^-24) |a| |b| (rounding
       // of both operands, u = 2^-11, and of the fp32 accumulation) plus
       // 2^-25 sqrt(d) (|a| + |b|) for operands in fp16's subnormal range; L2
-      // adds the rounding of "dot - |b|^2"; doubled for safety
-      const double na = std::sqrt((double)nq2) * 1.001 * std::ldexp(1.0, eq);
-      const double nbn = std::sqrt((double)nb2) * 1.001 * std::ldexp(1.0, eb);
-      const double u = std::ldexp(1.0, -11);
-      double e = (2 * u + u * u + (d + 16) * std::ldexp(1.0, -24)) * na * nbn +
-                 std::ldexp(1.0, -25) * std::sqrt((double)d) * (na + nbn);
-      if (l2) e += std::ldexp(1.0, -23) * (na * nbn + (double)nb2 * 1.001 * std::ldexp(1.0, eb + eq));
-      const float eps = (float)(2.0 * e);
+      // adds the rounding of "dot - |b|^2"; doubled for safety.  In the
+      // operands' scaled units (scales 2^xb, 2^xq).
+      auto bound = [&](int xb, int xq) {
+        const double na = std::sqrt((double)nq2) * 1.001 * std::ldexp(1.0, xq);
+        const double nbn = std::sqrt((double)nb2) * 1.001 * std::ldexp(1.0, xb);
+        const double u = std::ldexp(1.0, -11);
+        double e = (2 * u + u * u + (d + 16) * std::ldexp(1.0, -24)) * na * nbn +
+                   std::ldexp(1.0, -25) * std::sqrt((double)d) * (na + nbn);
+        if (l2)
+          e += std::ldexp(1.0, -23) * (na * nbn + (double)nb2 * 1.001 * std::ldexp(1.0, xb + xq));
+        return 2.0 * e;
+      };
+      // The first prep pass wrote the operands at scale 1 (and |b|^2, |q|^2
+      // for it).  Keep them when they are clear of fp16's overflow and the
+      // bound at scale 1 is within 1 % of the bound at the best scales, in
+      // unscaled units (unit rows: the subnormal term is about 2e-6 of the
+      // rounding term), which saves a second pass over the base.
+      const double qmul = l2 ? 2.0 : 1.0;
+      const bool keep = amax_b < 16384.0f && qmul * amax_q < 16384.0 &&
+                        bound(0, 0) <= 1.01 * bound(eb, eq) * std::ldexp(1.0, -(eb + eq));
+      // the one-pass scales (the split passes below always use eb, eq)
+      const int xb = keep ? 0 : eb, xq = keep ? 0 : eq;
+      if (!keep) {
+        const float sb = std::ldexp(1.0f, eb), sq = std::ldexp(1.0f, eq);
+        PrepParams pb1{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, nullptr,
+                       nb, l2 ? std::ldexp(1.0f, eb + eq) : 0.0f, INFINITY, nullptr, nullptr,
+                       nullptr};
+        PrepParams pq1{queries, nq, nq_pad, d, d_pad, cosine ? 1 : 0, l2 ? 2.0f : 1.0f, sq,
+                       q_hi, nullptr, nullptr, 0.0f, 0.0f, nullptr, nullptr, nullptr};
+        launch_prep(pb1, dev.sms, s);
+        launch_prep(pq1, dev.sms, s);
+      }
+      const float eps = (float)bound(xb, xq);
       if (approx_search(base, n, queries, nq, d, k, mi, id_offset, self_base, b_hi, q_hi, nb, qq,
                         n_pad, nq_pad, d_pad, kchunks, l2 ? 0 : 1, eps, out_keys, ids, dist, sc,
                         s))
         return;
     }
+    const float sb = std::ldexp(1.0f, eb), sq = std::ldexp(1.0f, eq);
     b_lo = sc.alloc<__half>((size_t)n_pad * d_pad);
     q_lo = sc.alloc<__half>((size_t)nq_pad * d_pad);
     PrepParams pb2{base, n, n_pad, d, d_pad, cosine ? 1 : 0, 1.0f, sb, b_hi, b_lo,

@@ -805,37 +805,28 @@ __global__ void __launch_bounds__(GemmLayout<QB, NPASS, CG>::THREADS, 1)
             }
           }
         } else {
+        // 64 columns per round trip to TMEM: two loads in flight, one wait
         uint32_t ra[32], rb[32];
-        tmem_ld32(taddr, ra);
-        tmem_wait_ld_regs(ra);
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
           __syncwarp();
+          tmem_ld32(taddr + c * 32, ra);
           tmem_ld32(taddr + (c + 1) * 32, rb);
-          if constexpr (KR > 0 && NBM == 1 && MODE == 0) {
-            epi_sub32<NBM, KR, OP, MODE>(ra, nbw + c * 32, col_base + c * 32, p, row_on, key, sv, st);
-          } else {
-            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
-            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
-          }
-          __syncwarp();
-          tmem_wait_ld_regs(rb);
-          if (c + 2 < NCH) {
-            tmem_ld32(taddr + (c + 2) * 32, ra);
-          } else {
+          tmem_wait_ld_regs(ra);
+          tmem_regs_ready(rb);
+          if (c + 2 >= NCH) {
             // the accumulator is free once its last columns are in registers
             tc_fence_before();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
           if constexpr (KR > 0 && NBM == 1 && MODE == 0) {
+            epi_sub32<NBM, KR, OP, MODE>(ra, nbw + c * 32, col_base + c * 32, p, row_on, key, sv, st);
             epi_sub32<NBM, KR, OP, MODE>(rb, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, key, sv, st);
           } else {
+            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 0, nbw + c * 32, col_base + c * 32, p, row_on, heap, key, sv, st);
+            epi_sub16<HS, NBM, KR, OP, MODE>(ra, 16, nbw + c * 32 + 16, col_base + c * 32 + 16, p, row_on, heap, key, sv, st);
             epi_sub16<HS, NBM, KR, OP, MODE>(rb, 0, nbw + c * 32 + 32, col_base + c * 32 + 32, p, row_on, heap, key, sv, st);
             epi_sub16<HS, NBM, KR, OP, MODE>(rb, 16, nbw + c * 32 + 48, col_base + c * 32 + 48, p, row_on, heap, key, sv, st);
-          }
-          if (c + 2 < NCH) {
-            __syncwarp();
-            tmem_wait_ld_regs(ra);
           }
         }
         }
