@@ -8,8 +8,10 @@ L2, k=10, 10k queries; base rows sharded across the GPUs of one node).
 
 A step is one exact search of every query against the whole base: the
 fp32 -> fp16 input conversion, the fused tcgen05 distance + top-k kernel,
-(for N > 1) the NCCL all-gather of each rank's [nq, k] candidates, and the
-merge to ids and distances.  `value` is whole-job queries/s with the inputs
+(for N > 1) the exchange of each rank's [nq, k] candidates (read from the
+peers' memory over NVLink; `--exchange nccl` for an NCCL all-gather), and
+the merge to ids and distances.  The topk-merge and refine workloads time
+those two callers of the search on one GPU against HBM bandwidth.  `value` is whole-job queries/s with the inputs
 resident in HBM, L2 flushed before every timed step (a rank's shard is
 smaller than L2 at 8 GPUs); `e2e` is the same through the host-memory API,
 copies included.
@@ -73,6 +75,16 @@ WORKLOADS = {
     "hamming-10m-1024b": dict(kind="hamming", n=10_000_000, nq=10_000, bytes=128, k=10,
                               prototypes=4096, flip=0.1,
                               desc="config 4: 10M x 1024-bit codes, 10k queries, k=10"),
+    # the callers either side of the search (not BASELINE configurations):
+    # one topk_merge step over 10k rows of 16,384 scores (655 MB, read once),
+    # and refine of 1,024 candidates per query over config 1's rows
+    "topk-merge-10k-t16384-k100": dict(kind="topk", n=16_384, nq=10_000, k=100,
+                                       desc="topk_merge: 10k rows x 16,384 integer-valued "
+                                            "float32 scores, k=100, first step"),
+    "refine-10k-c1024-k10": dict(kind="refine", n=1_000_000, nq=10_000, d=128, c=1024, k=10,
+                                 metric="l2", clusters=1024,
+                                 desc="refine: 10k queries x 1,024 random candidate rows of "
+                                      "config 1's 1M x 128 base, L2, k=10"),
 }
 DEFAULT_WORKLOAD = "knn-l2-1m-k10"
 # twice the B200's 126 MB L2
@@ -419,6 +431,85 @@ def check_parity(w, base, q, ids, dist, k, metric):
             "seconds": round(time.perf_counter() - t0, 2)}
 
 
+# ---------------------------------------------------------------- select arm
+
+def select_arm(args, w, peaks):
+    """topk_merge or refine on one GPU (rank 0 under torchrun): each step
+    timed with CUDA events after an L2 flush, its HBM bytes against the
+    measured copy bandwidth, and the first rows checked against the oracle."""
+    if env_int("RANK", 0) != 0:
+        return 0
+    import torch
+
+    import mlxvs_b200 as mv
+    from oracle import oracle as O
+
+    dev = torch.device("cuda", env_int("LOCAL_RANK", 0))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    k = w["k"]
+    if w["kind"] == "topk":
+        # integer-valued scores: many ties, which the reference's order breaks
+        scores = (torch.randn((w["nq"], w["n"]), generator=g, device=dev) * 64.0).round_()
+
+        def step():
+            return mv.topk_merge(scores, None, None, 0, True, k)
+
+        algo_bytes = scores.numel() * 4 + w["nq"] * k * 8
+        kname = "topk_rows"
+    else:
+        base = gen_mixture_torch(w["n"], w["d"], w["clusters"], 0, dev)
+        q = gen_mixture_torch(w["nq"], w["d"], w["clusters"], 1, dev)
+        cand = torch.randint(0, w["n"], (w["nq"], w["c"]), generator=g, device=dev)
+
+        def step():
+            return mv.refine(base, q, cand, k, w["metric"])
+
+        # every candidate row gathered once, its id, the queries
+        algo_bytes = w["nq"] * w["c"] * (w["d"] * 4 + 8) + w["nq"] * w["d"] * 4
+        kname = "refine"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    spans = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0x7F)
+        spans[i][0].record(stream)
+        out = step()
+        spans[i][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in spans) / args.steps
+    m = 200
+    ids = out[0][:m].cpu().numpy()
+    vals = out[1][:m].cpu().numpy()
+    if w["kind"] == "topk":
+        oi, ov = O.topk_merge(scores[:m].cpu().numpy(), None, None, 0, True, k)
+    else:
+        oi, ov = O.refine(base.cpu().numpy(), q[:m].cpu().numpy(), cand[:m].cpu().numpy(), k,
+                          w["metric"])
+    mism = int(np.sum(np.any(ids != oi, axis=1) | np.any(vals != ov, axis=1)))
+    gbs = algo_bytes / (ms / 1e3) / 1e9
+    line = {
+        "metric": f"{w['kind']} rows/s", "value": w["nq"] / (ms / 1e3), "unit": "rows/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "desc": w["desc"],
+                   "l2_flush": f"{FLUSH_BYTES >> 20} MiB buffer written before every step"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "kernel": kname,
+                     "algorithmic_per_step": f"{algo_bytes:.3e} bytes",
+                     "peak_source": f"{peaks['source']} copy bandwidth"},
+        "parity": {"checked": m, "of": w["nq"], "unit": "rows", "mismatched": mism,
+                   "rule": "ids and scores bit-exact", "against": "oracle/oracle.py"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- GPU arm
 
 def main():
@@ -450,6 +541,8 @@ def main():
     peaks = load_peaks()
     if args.impl == "reference":
         return reference_arm(args, w, peaks)
+    if w["kind"] in ("topk", "refine"):
+        return select_arm(args, w, peaks)
 
     import torch
     import torch.distributed as dist
