@@ -1315,9 +1315,10 @@ void refine(const float* dataset, int64_t n, int d, const float* queries, int64_
   {
     const int64_t pairs = nq * (int64_t)c;
     const int warps_per_block = 8;
-    require(pairs / warps_per_block < (1LL << 31), "[mlxvs::refine] too many candidates.");
+    const int64_t per_block = (int64_t)warps_per_block * REFINE_ROWS;
+    require(pairs / per_block < (1LL << 31), "[mlxvs::refine] too many candidates.");
     ProfScope prof("refine_scores", s);
-    refine_scores_kernel<<<(unsigned)((pairs + warps_per_block - 1) / warps_per_block),
+    refine_scores_kernel<<<(unsigned)((pairs + per_block - 1) / per_block),
                            warps_per_block * 32, 0, s>>>(rp);
     CK(cudaGetLastError());
   }

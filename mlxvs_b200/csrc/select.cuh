@@ -23,6 +23,34 @@ struct TopkRowsParams {
   float* out_scores;         // [nq][k]
 };
 
+// The radix select stops once its bucket holds at most this many entries
+// and sorts those instead.
+constexpr int TOPK_BUCKET = 256;
+
+// Sorts keys[0 .. n) in shared memory, largest first (a bitonic network
+// over the next power of two; the caller has zeroed the slots past n, and
+// zero is below every real key).  Every thread of the block calls it.
+__device__ __forceinline__ void bitonic_desc_u64(unsigned long long* keys, uint32_t n, int lid) {
+  uint32_t size_pow2 = 1;
+  while (size_pow2 < n) size_pow2 <<= 1;
+  for (uint32_t size = 2; size <= size_pow2; size <<= 1) {
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (uint32_t i = lid; i < size_pow2; i += TOPK_THREADS) {
+        const uint32_t j = i ^ stride;
+        if (j > i) {
+          const bool forward = (i & size) == 0;
+          const unsigned long long a = keys[i], b = keys[j];
+          if (forward != (a > b)) {
+            keys[i] = b;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // "a comes before b": higher score first, then lower id as unsigned (so -1
 // goes last); src/kernels.h:21-23.
 __device__ __forceinline__ bool topk_before(float sa, int32_t ia, float sb, int32_t ib) {
@@ -44,6 +72,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams 
   __shared__ uint32_t taken_above, taken_equal;
   __shared__ float sel_score[TOPK_KMAX];
   __shared__ int32_t sel_id[TOPK_KMAX];
+  __shared__ unsigned long long bucket[TOPK_BUCKET];
+  __shared__ uint32_t s_count, n_bucket;
 
   const int lid = threadIdx.x;
   const int warp = lid >> 5;
@@ -72,6 +102,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams 
 
   uint64_t prefix = 0, mask = 0;
   uint32_t need = keff;
+  bool compact = false;
   if (keff > 0) {
     for (int shift = 56; shift >= 0; shift -= 8) {
       for (int i = lid; i < WARPS * 256; i += TOPK_THREADS) (&hist[0][0])[i] = 0u;
@@ -103,27 +134,33 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams 
         s_prefix = prefix | ((uint64_t)lid << shift);
         s_need = need - above;
         s_done = (c == need - above) ? 1u : 0u;
+        s_count = c;
       }
       __syncthreads();
       prefix = s_prefix;
       need = s_need;
       mask |= 255ull << shift;
       const bool done = s_done != 0;
+      compact = !done && s_count <= (uint32_t)TOPK_BUCKET;
       __syncthreads();
-      if (done) break;
+      if (done || compact) break;
     }
   }
 
   // gather: every key above the k-th, and `need` of those equal to it (equal
-  // keys are equal entries, so which of them is immaterial)
+  // keys are equal entries, so which of them is immaterial); when the
+  // selected bucket is small, its keys instead, whose best `need` a sort in
+  // shared memory picks (instead of more passes over the row)
   if (lid == 0) {
     taken_above = 0;
     taken_equal = 0;
+    n_bucket = 0;
   }
   for (int i = lid; i < TOPK_KMAX; i += TOPK_THREADS) {
     sel_score[i] = -INFINITY;
     sel_id[i] = -1;
   }
+  for (int i = lid; i < TOPK_BUCKET; i += TOPK_THREADS) bucket[i] = 0ull;
   __syncthreads();
   const uint32_t n_above = keff - need;
   if (keff > 0) {
@@ -131,21 +168,35 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_rows_kernel(TopkRowsParams 
       float v;
       int32_t id;
       candidate(i, v, id);
-      const uint64_t key = key_of(v, id) & mask;
+      const uint64_t full = key_of(v, id);
+      const uint64_t key = full & mask;
       if (key > prefix) {
         const uint32_t at = atomicAdd(&taken_above, 1u);
         sel_score[at] = v;
         sel_id[at] = id;
       } else if (key == prefix) {
-        const uint32_t at = atomicAdd(&taken_equal, 1u);
-        if (at < need) {
-          sel_score[n_above + at] = v;
-          sel_id[n_above + at] = id;
+        if (compact) {
+          bucket[atomicAdd(&n_bucket, 1u)] = full;
+        } else {
+          const uint32_t at = atomicAdd(&taken_equal, 1u);
+          if (at < need) {
+            sel_score[n_above + at] = v;
+            sel_id[n_above + at] = id;
+          }
         }
       }
     }
   }
   __syncthreads();
+  if (compact) {
+    bitonic_desc_u64(bucket, n_bucket, lid);
+    for (uint32_t i = lid; i < need; i += TOPK_THREADS) {
+      const uint64_t key = bucket[i];
+      sel_score[n_above + i] = from_order_bits((uint32_t)(key >> 32));
+      sel_id[n_above + i] = (int32_t)(~(uint32_t)key);
+    }
+    __syncthreads();
+  }
 
   // bitonic sort of the winners, best first (src/kernels.h:196-222)
   uint32_t size_pow2 = 1;
@@ -427,55 +478,84 @@ struct RefineParams {
   float* scores;              // [nq][c]: larger is closer, -inf where invalid
 };
 
-// One warp per (query, candidate): the exact score of the candidate row as
-// the reference computes it (src/ivf.cpp:1677-1690): L2 -sum((r - q)^2),
-// inner product sum(r q), cosine on rows and query divided by
-// max(norm, 1e-30).  Ids outside [0, n) score -inf.
+// One warp per REFINE_ROWS (query, candidate) pairs: the exact score of each
+// candidate row as the reference computes it (src/ivf.cpp:1677-1690): L2
+// -sum((r - q)^2), inner product sum(r q), cosine on rows and query divided
+// by max(norm, 1e-30).  Ids outside [0, n) score -inf.  The rows' loads are
+// issued together (a gather is latency-bound: one 512-byte row per warp
+// leaves most of the memory system idle); each pair's sum runs in the same
+// order as with one pair per warp.
+constexpr int REFINE_ROWS = 4;
+
 __global__ void refine_scores_kernel(RefineParams p) {
   const int lane = threadIdx.x & 31;
-  const int64_t pair = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (pair >= p.nq * (int64_t)p.c) return;
-  const int64_t q = pair / p.c;
-  const int32_t id = p.candidates[pair];
-  if (id < 0 || (int64_t)id >= p.n) {
-    if (lane == 0) p.scores[pair] = -INFINITY;
-    return;
+  const int64_t total = p.nq * (int64_t)p.c;
+  const int64_t first =
+      ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * REFINE_ROWS;
+  if (first >= total) return;
+  const float* r[REFINE_ROWS];
+  const float* x[REFINE_ROWS];
+  bool on[REFINE_ROWS], valid[REFINE_ROWS];
+#pragma unroll
+  for (int t = 0; t < REFINE_ROWS; ++t) {
+    const int64_t pair = first + t;
+    on[t] = pair < total;
+    const int32_t id = on[t] ? p.candidates[pair] : -1;
+    valid[t] = on[t] && id >= 0 && (int64_t)id < p.n;
+    r[t] = p.dataset + (valid[t] ? (int64_t)id * p.d : 0);
+    x[t] = p.queries + (on[t] ? pair / p.c : 0) * p.d;
   }
-  const float* r = p.dataset + (int64_t)id * p.d;
-  const float* x = p.queries + q * p.d;
-  float acc = 0.0f, rr = 0.0f, xx = 0.0f;
+  float acc[REFINE_ROWS], rr[REFINE_ROWS], xx[REFINE_ROWS];
+#pragma unroll
+  for (int t = 0; t < REFINE_ROWS; ++t) acc[t] = rr[t] = xx[t] = 0.0f;
   for (int j = lane; j < p.d; j += 32) {
-    const float a = __ldg(r + j);
-    const float b = __ldg(x + j);
-    if (p.metric == 1) {
-      const float df = a - b;
-      acc = fmaf(df, df, acc);
-    } else {
-      acc = fmaf(a, b, acc);
-      if (p.metric == 2) {
-        rr = fmaf(a, a, rr);
-        xx = fmaf(b, b, xx);
+    float a[REFINE_ROWS], bq[REFINE_ROWS];
+#pragma unroll
+    for (int t = 0; t < REFINE_ROWS; ++t) {
+      a[t] = valid[t] ? __ldg(r[t] + j) : 0.0f;
+      bq[t] = valid[t] ? __ldg(x[t] + j) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < REFINE_ROWS; ++t) {
+      if (p.metric == 1) {
+        const float df = a[t] - bq[t];
+        acc[t] = fmaf(df, df, acc[t]);
+      } else {
+        acc[t] = fmaf(a[t], bq[t], acc[t]);
+        if (p.metric == 2) {
+          rr[t] = fmaf(a[t], a[t], rr[t]);
+          xx[t] = fmaf(bq[t], bq[t], xx[t]);
+        }
       }
     }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (p.metric == 2) {
-      rr += __shfl_xor_sync(0xffffffffu, rr, off);
-      xx += __shfl_xor_sync(0xffffffffu, xx, off);
+  for (int t = 0; t < REFINE_ROWS; ++t) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], off);
+      if (p.metric == 2) {
+        rr[t] += __shfl_xor_sync(0xffffffffu, rr[t], off);
+        xx[t] += __shfl_xor_sync(0xffffffffu, xx[t], off);
+      }
     }
   }
   if (lane == 0) {
-    float s;
-    if (p.metric == 1) {
-      s = -acc;
-    } else if (p.metric == 2) {
-      s = acc / (fmaxf(sqrtf(rr), 1e-30f) * fmaxf(sqrtf(xx), 1e-30f));
-    } else {
-      s = acc;
+#pragma unroll
+    for (int t = 0; t < REFINE_ROWS; ++t) {
+      if (!on[t]) continue;
+      float sc;
+      if (!valid[t]) {
+        sc = -INFINITY;
+      } else if (p.metric == 1) {
+        sc = -acc[t];
+      } else if (p.metric == 2) {
+        sc = acc[t] / (fmaxf(sqrtf(rr[t]), 1e-30f) * fmaxf(sqrtf(xx[t]), 1e-30f));
+      } else {
+        sc = acc[t];
+      }
+      p.scores[first + t] = sc;
     }
-    p.scores[pair] = s;
   }
 }
 
