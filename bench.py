@@ -323,7 +323,7 @@ def cpu_sample_rate(w, base_np, q_np, budget_s, threads=0):
         m = min(q_np.shape[0], m * 4)
         t = run(m)
     rate = m / t
-    m2 = int(min(q_np.shape[0], max(m, rate * budget_s)))
+    m2 = int(min(q_np.shape[0], max(1, rate * budget_s)))
     t2 = run(m2) if m2 != m else t
     return m2 / t2, m2, t2
 
@@ -340,8 +340,8 @@ def reference_arm(args, w, peaks):
     base, q = make_inputs(w, "cpu")
     base_np, q_np = base.numpy(), q.numpy()
     # each step: a bounded sample of the workload (all base rows, the first
-    # m queries), m chosen so the whole run stays within a few minutes
-    per_step = max(0.05, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
+    # m queries), m chosen so that the steps take about 90 s in all
+    per_step = max(0.05, min(2.0, 90.0 / max(1, args.steps + args.warmup)))
     rate, m, _ = cpu_sample_rate(w, base_np, q_np, per_step, threads=cores)
     from oracle import oracle as O
 
